@@ -1,0 +1,484 @@
+#!/usr/bin/env python
+"""Benchmark of B200 paged decode attention (xLLMs' decode hot path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c2|c1|c3|c4|c5]
+
+One step = one decode-attention pass over the whole batch (one new token per
+sequence). N = 1 runs BASELINE config 2 (Llama-3-8B GQA, B = 64, fp16 KV,
+context U[1024, 8192]). With N > 1 (launched by torch.distributed.run, one
+rank per GPU) the batch grows to 64*N sequences and the 8 KV heads are
+sharded over the ranks (KV-head-group sharding): per-GPU work stays that of
+config 2 ("scaling": "weak"), each rank holds its own page pool and block
+tables, and the outputs are all-gathered over NCCL into [B, Hq, D].
+
+Printed by rank 0: one JSON line. `value` is algorithmic GB/s of the whole
+job (KV + Q + out + block tables + seq_lens) with inputs resident in HBM,
+device-timed with CUDA events, max over ranks. `e2e` is the same metric
+through the backend plugin's C ABI with Q / block tables / seq_lens copied
+host->device and the output device->host inside every step. `roofline`
+covers the attention kernel alone (events recorded around it by the
+library). `cpu_baseline` times the reference's CPU attention on the host.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "paged-decode KV-read GB/s (% of HBM peak) & seq-tokens/s at 1/2/4/8 GPU"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--cpu-seconds", type=float, default=6.0,
+                    help="wall-time budget of the cpu_baseline leg")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def make_batch(workload: str, world: int, rank: int):
+    from xllms_b200 import workloads as W
+    if workload == "c2":
+        return W.config2(num_seqs=64 * world, world_size=world, rank=rank)
+    if workload == "c5":
+        return W.config5(world_size=world, rank=rank)
+    if world > 1:
+        raise SystemExit(f"workload {workload} runs on one GPU")
+    return W.CONFIGS[workload]()
+
+
+# ── clocks during the timed region ────────────────────────────────────────
+_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+            0x2: "applications_clocks_setting", 0x10: "sync_boost"}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons of one GPU through NVML."""
+
+    def __init__(self, torch_device: int, period_s: float = 0.01):
+        self.period = period_s
+        self.samples = []
+        self.max_mhz = None
+        self.err = None
+        self._stop = threading.Event()
+        self._thr = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            p = torch.cuda.get_device_properties(torch_device)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # pragma: no cover - depends on the box
+            self.err = f"nvml unavailable: {exc}"
+            self.h = None
+
+    def _reasons(self):
+        nv = self.nv
+        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        return int(fn(self.h))
+
+    def _run(self):
+        while not self._stop.is_set():
+            self.sample()
+            time.sleep(self.period)
+
+    def sample(self):
+        if self.h is None:
+            return
+        try:
+            mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+            self.samples.append((mhz, self._reasons()))
+        except Exception as exc:  # pragma: no cover
+            self.err = str(exc)
+
+    def start(self):
+        if self.h is not None:
+            self.sample()
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+
+    def stop(self):
+        if self._thr is not None:
+            self._stop.set()
+            self._thr.join()
+        self.sample()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
+                    "samples": 0, "note": self.err or "no samples"}
+        reasons = 0
+        for _, r in self.samples:
+            reasons |= r
+        names = sorted({n for bit, n in _REASONS.items() if reasons & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+# ── CPU baseline: the reference's own CPU attention on the host cores ─────
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def sample_arrays(batch, nseq, q_t=None, k_t=None, v_t=None):
+    """Host arrays (q, k, v, block_tables, seq_lens) of the first `nseq`
+    sequences with their pages renumbered compactly: copied from the device
+    pools when given, else drawn on the host (numpy PCG64, the batch's seed)."""
+    import numpy as np
+    seqs = list(range(min(nseq, batch.num_seqs)))
+    if q_t is not None:
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        from _helpers import gather_subset
+        return gather_subset(batch, seqs, q_t, k_t, v_t)
+    from xllms_b200 import workloads as W
+    sub = W.make_batch(batch.name + "_sample", batch.seq_lens[seqs], batch.num_heads,
+                       batch.num_kv_heads, batch.head_size, batch.dtype, batch.seed,
+                       block_size=batch.block_size, slack=0.0, value_std=batch.value_std)
+    q, k, v = sub.values_numpy()
+    return q, k, v, sub.block_tables, sub.seq_lens
+
+
+def cpu_leg(batch, arrays, seconds: float = 0.0, passes: int = 0, warmup: int = 1):
+    """Times the reference CPU path (oracle/_ref, else the oracle port) over the
+    sample `arrays` on all host cores. Returns (GB/s, seconds per pass, info)."""
+    import numpy as np
+    from oracle import oracle as O
+    q, k, v, bt, sl = arrays
+    nseq = len(sl)
+    cores = host_cores()
+    sub_bytes = int(sl.astype(np.int64).sum()) * batch.num_kv_heads * \
+        batch.head_size * 2 * batch.elem_size
+    sub_bytes += 2 * nseq * batch.num_heads * batch.head_size * batch.elem_size
+    sub_bytes += int(((sl.astype(np.int64) + 15) // 16).sum()) * 4 + 4 * nseq
+    if O.ref_available():
+        kind = "reference"
+        kr, vr = O.to_run_gpt2_layout(k, v, batch.num_kv_heads, batch.num_heads,
+                                      batch.block_size)
+        pt = O.per_token_tables(bt, sl, batch.block_size)
+        qf = q.astype(np.float32)
+
+        def one():
+            O.reference_attention(qf, kr, vr, pt, sl, batch.block_size, threads=cores)
+        what = ("xLLMs examples/run_gpt2.c paged_attention (fp32, GQA via repeated KV heads), "
+                "OpenMP over sequences")
+    else:
+        kind = "port"
+
+        def one():
+            O.attention(q, k, v, bt, sl, batch.num_kv_heads, batch.scale, threads=cores)
+        what = "oracle/pa_oracle.c restatement, OpenMP over (seq, head)"
+    for _ in range(max(1, warmup)):
+        one()
+    times = []
+    t_end = time.perf_counter() + seconds
+    while (passes and len(times) < passes) or (not passes and
+                                                 (not times or time.perf_counter() < t_end)):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    per = statistics.mean(times)
+    info = {"kind": kind, "cores": cores,
+            "sample": f"first {nseq} of {batch.num_seqs} sequences "
+                      f"({int(sl.sum())} context tokens, {sub_bytes / 1e6:.1f} MB algorithmic); "
+                      f"{what}; {len(times)} timed passes"}
+    return sub_bytes / per / 1e9, per, info
+
+
+# ── our implementation ─────────────────────────────────────────────────────
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from xllms_b200 import _native
+    from xllms_b200 import operator_api as PA
+    from xllms_b200 import sharding
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    batch = make_batch(args.workload, world, rank)
+    q, k, v = batch.values_torch(dev)
+    bt, sl = batch.tables_torch(dev)
+    out = torch.empty_like(q)
+    gathered = full = None
+    if world > 1:
+        gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
+        full = torch.empty((batch.num_seqs, batch.total_heads, batch.head_size),
+                           dtype=out.dtype, device=dev)
+    lib = _native.xpa()
+    path = PA.kernel_path(k, v, batch.num_heads, batch.head_size, batch.num_kv_heads,
+                          batch.block_size, batch.dtype_size, batch.kv_block_stride,
+                          batch.kv_head_stride)
+    split = PA.workspace_size(batch.num_seqs, batch.num_heads, batch.head_size,
+                              batch.num_kv_heads, batch.max_blocks, batch.block_size,
+                              batch.dtype_size) > 0
+    launches_per_step = 1 + (1 if split else 0)
+
+    def step():
+        PA.paged_attention(q, k, v, bt, sl, out=out, num_blocks=batch.num_blocks)
+        if world > 1:
+            sharding.gather_heads(out, gathered)
+            sharding.interleave_heads(gathered, full)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    st = PA.device_status(clear=True)
+    if st:
+        raise SystemExit(f"device status after warm-up: {st:#x}")
+
+    K = args.steps
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    for e in ev_a + ev_b:
+        e.record()  # materialise the CUDA event handles
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local_rank)
+    barrier()
+    clocks.start()
+    start.record()
+    for i in range(K):
+        lib.nxt_paged_attention_profile_next(ev_a[i].cuda_event, ev_b[i].cuda_event)
+        step()
+    stop.record()
+    barrier()
+    clocks.stop()
+    t_step = start.elapsed_time(stop) / K
+    t_kern = statistics.mean(a.elapsed_time(b) for a, b in zip(ev_a, ev_b))
+    st = PA.device_status(clear=True)
+    if st:
+        raise SystemExit(f"device status after timing: {st:#x}")
+
+    # ── e2e through the backend plugin (C ABI) with host buffers ───────────
+    plugin = PA.CudaBackendPlugin()
+    q_h = q.cpu().pin_memory()
+    bt_h = bt.cpu().pin_memory()
+    sl_h = sl.cpu().pin_memory()
+    q_d, bt_d, sl_d = torch.empty_like(q), torch.empty_like(bt), torch.empty_like(sl)
+    out_d = torch.empty_like(out)
+    res = full if world > 1 else out_d
+    out_h = torch.empty(res.shape, dtype=res.dtype).pin_memory()
+    pa_in = PA.make_input(q_d, k, v, bt_d, sl_d, scale=batch.scale,
+                          stream=torch.cuda.current_stream())
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        bt_d.copy_(bt_h, non_blocking=True)
+        sl_d.copy_(sl_h, non_blocking=True)
+        if plugin.run(pa_in, out_d) != 0:
+            raise SystemExit("nxt_backend_run failed")
+        if world > 1:
+            sharding.gather_heads(out_d, gathered)
+            sharding.interleave_heads(gathered, full)
+        out_h.copy_(res, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks_e2e = ClockSampler(local_rank)
+    clocks_e2e.start()
+    e_start.record()
+    for _ in range(K):
+        e2e_step()
+    e_stop.record()
+    barrier()
+    clocks_e2e.stop()
+    t_e2e = e_start.elapsed_time(e_stop) / K
+    if not torch.equal(out_h.to(dev), res):
+        raise SystemExit("e2e output differs from the device-resident run")
+    plugin.close()
+
+    bytes_rank = batch.algorithmic_bytes()
+    ub_rank = batch.algorithmic_bytes(unique=True) if args.workload == "c4" else bytes_rank
+    kv_rank = batch.kv_bytes()
+    h2d = (q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + sl_h.numel() * 4)
+    d2h = out_h.numel() * out_h.element_size()
+    if world > 1:
+        t = torch.tensor([t_step, t_kern, t_e2e], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_step, t_kern, t_e2e = (float(x) for x in t.tolist())
+        s = torch.tensor([bytes_rank, ub_rank, kv_rank, h2d, d2h], dtype=torch.float64,
+                         device=dev)
+        dist.all_reduce(s, op=dist.ReduceOp.SUM)
+        tot_bytes, tot_ub, tot_kv, h2d, d2h = (float(x) for x in s.tolist())
+    else:
+        tot_bytes, tot_ub, tot_kv = float(bytes_rank), float(ub_rank), float(kv_rank)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, per, info = cpu_leg(batch, sample_arrays(batch, 8, q, k, v), args.cpu_seconds)
+        cpu = dict(value=round(gbs, 3), unit="GB/s", **info)
+
+    if rank != 0:
+        return None
+    peak, peak_src = hbm_peak()
+    value = tot_bytes / (t_step * 1e-3) / 1e9
+    kern_gbs = ub_rank / (t_kern * 1e-3) / 1e9  # per GPU: the kernel's own bytes per launch
+    seqs_total = batch.num_seqs  # every rank decodes every sequence for its heads
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic: seeded block tables/lengths (numpy PCG64); Q/K/V N(0,1)*std "
+                "drawn on the device (torch CUDA generator)",
+        "config": {
+            "workload": batch.name,
+            "num_seqs": batch.num_seqs,
+            "num_heads": batch.total_heads,
+            "num_kv_heads": batch.num_kv_heads * world,
+            "kv_heads_per_gpu": batch.num_kv_heads,
+            "head_size": batch.head_size,
+            "block_size": batch.block_size,
+            "max_blocks_per_seq": batch.max_blocks,
+            "context_tokens": batch.context_tokens(),
+            "parallelism": "single GPU" if world == 1 else
+                           f"KV-head sharding x{world} + NCCL all-gather of outputs",
+            "l2": f"no flush: each step reads {tot_kv / world / 1e9:.2f} GB of KV per GPU "
+                  f"(> {L2_BYTES >> 20} MB L2)",
+            "path": {1: "tma_mma", 2: "generic"}.get(path, "none"),
+        },
+        "pct_hbm_peak": round(100.0 * (tot_ub / world) / (t_step * 1e-3) / 1e9 / peak, 2),
+        "seq_tokens_per_s": round(seqs_total / (t_step * 1e-3), 1),
+        "context_tokens_per_s": round(batch.context_tokens() / (t_step * 1e-3), 1),
+        "kv_gbs": round(tot_kv / (t_step * 1e-3) / 1e9, 2),
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "pa_tma_mma_kernel" if path == 1 else "pa_generic_kernel",
+            "achieved": round(kern_gbs, 2),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(kern_gbs / peak, 4),
+            "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
+                           else "fallback 6.65 TB/s",
+            "kernel_ms": round(t_kern, 5),
+            "traffic": None,
+            "bytes_per_launch": ub_rank,
+        },
+        "e2e": {
+            "value": round(tot_bytes / (t_e2e * 1e-3) / 1e9, 2),
+            "unit": "GB/s",
+            "ms_per_step": round(t_e2e, 5),
+            "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h),
+            "api": "nxt_backend_run (libxllm_cuda_backend.so) + pinned-host copies",
+            "clocks": clocks_e2e.summary(),
+        },
+        "clocks": clocks.summary(),
+        "gpu_launches": launches_per_step * K * world,
+        "gpu_launches_per_rank": launches_per_step * K,
+    }
+    if args.workload == "c4":
+        line["unique_kv_gbs"] = round(tot_ub / (t_step * 1e-3) / 1e9, 2)
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+def run_reference(args, rank, world):
+    """The reference's own CPU attention on the host cores, on a sample of this
+    arm's workload (the first 8 sequences); rank 0 only, one sample pass per step."""
+    if rank != 0:
+        return None
+    batch = make_batch(args.workload, world, 0)
+    seqs = min(8, batch.num_seqs)
+    arrays = sample_arrays(batch, seqs)
+    gbs, per, info = cpu_leg(batch, arrays, passes=max(1, args.steps), warmup=args.warmup)
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(per * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic, the ours arm's seeded workload (first 8 sequences, host-drawn values)",
+        "config": {"workload": batch.name, "sample_seqs": seqs, "num_heads": batch.total_heads,
+                   "num_kv_heads": batch.num_kv_heads * world, "head_size": batch.head_size,
+                   "block_size": batch.block_size},
+        "seq_tokens_per_s": round(seqs / per, 2),
+        "cpu_baseline": dict(value=round(gbs, 3), unit="GB/s", **info),
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if args.gpus != 1 or world != 1:
+            print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

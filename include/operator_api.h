@@ -1,0 +1,181 @@
+/*
+ * operator_api.h — paged decode attention, C ABI of libxpa.so.
+ *
+ * Drop-in for the xLLMs operator header (include/operator_api.h of the xLLMs
+ * project): the three attention entry points keep their names, argument order,
+ * argument meaning and `void` return, and all of them have C linkage. Behind
+ * them sit hand-written sm_100a kernels (xllms_b200/csrc). Additions are
+ * marked "extension" and have no counterpart in the reference header.
+ *
+ * Layout contract (identical to the reference):
+ *   out, query   [num_seqs][num_heads][head_size], element type by dtype_size
+ *   key_cache,   element (page, kv_head, slot, d) at
+ *   value_cache    page*kv_block_stride + kv_head*kv_head_stride + slot*head_size + d
+ *   block_tables [num_seqs][max_num_blocks_per_seq] int32 physical page ids;
+ *                token t of sequence b lives in page block_tables[b][t / block_size]
+ *                at slot t % block_size
+ *   seq_lens     [num_seqs] int32 context lengths
+ *   query head h reads KV head h / (num_heads / num_kv_heads)
+ *   dtype_size   2 = fp16, 4 = fp32, for query, caches and out alike
+ * All pointers are device pointers; every call is asynchronous on `stream`
+ * (NULL = the legacy default stream) and the caller synchronises.
+ *
+ * Behaviour the reference leaves undefined, defined here:
+ *   - block_size is honoured (the reference kernels hard-code 16);
+ *   - a block-table entry < 0 (or >= num_blocks when the _ex call gives it)
+ *     masks that page's tokens out of the softmax and raises
+ *     NXT_PA_DEV_BAD_PAGE in the device status word;
+ *   - seq_len is clamped to [0, max_num_blocks_per_seq*block_size]
+ *     (NXT_PA_DEV_SEQ_CLAMPED when clamping happened);
+ *   - seq_len == 0 writes an all-zero output row (as the reference's inv_sum = 0);
+ *   - an unsupported shape or dtype launches nothing and records NXT_PA_EINVAL
+ *     (read it with nxt_paged_attention_last_error) instead of silently falling
+ *     back to another head size.
+ */
+#ifndef XPA_OPERATOR_API_H_
+#define XPA_OPERATOR_API_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Opaque stream handle: a cudaStream_t cast to void* (reference operator_api.h:29). */
+typedef void *nxt_stream_t;
+
+/* Replaces nxt_paged_attention (reference include/operator_api.h:63-72,
+ * operators/page_attention.cu:170). Supported: dtype_size 2 or 4, any
+ * head_size in 1..256, any num_heads that is a multiple of num_kv_heads. */
+void nxt_paged_attention(
+    void *out, const void *query,
+    const void *key_cache, const void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq,
+    int block_size, int dtype_size,
+    int kv_block_stride, int kv_head_stride,
+    nxt_stream_t stream);
+
+/* Replaces nxt_paged_attention_v2 (reference include/operator_api.h:84-93,
+ * operators/page_attention_v2.cu:262). Same computation and kernels as above. */
+void nxt_paged_attention_v2(
+    void *out, const void *query,
+    const void *key_cache, const void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq,
+    int block_size, int dtype_size,
+    int kv_block_stride, int kv_head_stride,
+    nxt_stream_t stream);
+
+/* Replaces nxt_paged_attention_flash (reference include/operator_api.h:106-115,
+ * operators/flashinfer_adapter.cu:329, built there only with USE_FLASHINFER;
+ * always exported here). Same computation and kernels as above. */
+void nxt_paged_attention_flash(
+    void *out, const void *query,
+    const void *key_cache, const void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq,
+    int block_size, int dtype_size,
+    int kv_block_stride, int kv_head_stride,
+    nxt_stream_t stream);
+
+/* ── extension: status codes ──────────────────────────────────────────── */
+#define NXT_PA_OK              0
+#define NXT_PA_EINVAL        (-22) /* unsupported or inconsistent arguments   */
+#define NXT_PA_ENOMEM        (-12) /* workspace allocation failed             */
+#define NXT_PA_EWORKSPACE    (-28) /* caller workspace smaller than required  */
+#define NXT_PA_ECUDA         (-5)  /* a CUDA runtime/driver call failed       */
+
+/* Device status word bits (set by the kernels, read by
+ * nxt_paged_attention_device_status). */
+#define NXT_PA_DEV_TIMEOUT     0x1 /* a bounded pipeline wait expired          */
+#define NXT_PA_DEV_BAD_PAGE    0x2 /* a block-table entry was masked           */
+#define NXT_PA_DEV_SEQ_CLAMPED 0x4 /* a seq_len was outside [0, max_blocks*block_size] */
+
+/* Kernel paths (nxt_paged_attention_path). */
+#define NXT_PA_PATH_NONE       0
+#define NXT_PA_PATH_TMA_MMA    1 /* fp16, block_size 16, head_size 64/128/256 */
+#define NXT_PA_PATH_GENERIC    2 /* every other supported shape               */
+
+/* extension — status of the last drop-in call (nxt_paged_attention{,_v2,_flash})
+ * made by the calling host thread: NXT_PA_OK or a negative code. */
+int nxt_paged_attention_last_error(void);
+
+/* extension — human-readable text for a status code. */
+const char *nxt_paged_attention_strerror(int code);
+
+/* extension — status-returning form of the calls above.
+ *   num_blocks        pages in each cache pool; > 0 lets the kernels mask
+ *                     entries >= num_blocks, <= 0 means unknown.
+ *   workspace         device memory for split-context partials, at least
+ *                     nxt_paged_attention_workspace_size(...) bytes, or NULL
+ *                     to use the library's per-(device, stream) workspace,
+ *                     which is allocated on first use and grown as needed.
+ *   device_status     device int the kernels OR their NXT_PA_DEV_* bits into,
+ *                     or NULL for the library's per-device status word.
+ * Returns NXT_PA_OK once the kernels are enqueued, else a negative code.
+ * Partials of one call live in the workspace until the call's kernels finish,
+ * so concurrent calls need distinct workspaces. */
+int nxt_paged_attention_ex(
+    void *out, const void *query,
+    const void *key_cache, const void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq,
+    int block_size, int dtype_size,
+    int64_t kv_block_stride, int64_t kv_head_stride,
+    int64_t num_blocks,
+    void *workspace, size_t workspace_bytes,
+    int *device_status,
+    nxt_stream_t stream);
+
+/* extension — bytes of workspace a call with these arguments needs (0 when
+ * no sequence can span more than one context partition). */
+size_t nxt_paged_attention_workspace_size(
+    int num_seqs, int num_heads, int head_size, int num_kv_heads,
+    int max_num_blocks_per_seq, int block_size, int dtype_size);
+
+/* extension — kernel path a call with these arguments takes (NXT_PA_PATH_*),
+ * NXT_PA_PATH_NONE when the arguments are unsupported. Pointer alignment is
+ * checked too, so pass the real cache pointers. */
+int nxt_paged_attention_path(
+    const void *key_cache, const void *value_cache,
+    int num_heads, int head_size, int num_kv_heads,
+    int block_size, int dtype_size,
+    int64_t kv_block_stride, int64_t kv_head_stride);
+
+/* extension — reads (and with clear != 0 resets) the current device's library
+ * status word. Synchronises the device. Returns the NXT_PA_DEV_* bits, or a
+ * negative code. */
+int nxt_paged_attention_device_status(int clear);
+
+/* extension — frees the library-owned workspaces and status words of every
+ * device. Synchronises each device that has one. */
+int nxt_paged_attention_release_workspaces(void);
+
+/* extension — instrumentation for timing the attention kernel alone. The next
+ * call made by this host thread records `before` on its stream immediately
+ * before the main attention kernel and `after` immediately after it (ahead of
+ * the split-context reduce). Both are cudaEvent_t values cast to void*; the
+ * request is consumed by that one call. NULL, NULL cancels a pending request. */
+int nxt_paged_attention_profile_next(void *before, void *after);
+
+/* extension — the calling thread's current CUDA device: its ordinal, SM count
+ * and name (name_len bytes at most, NUL-terminated). Used by the backend
+ * plugin's init. Returns NXT_PA_OK, or NXT_PA_ECUDA when no device is usable. */
+int nxt_paged_attention_device_info(int *device_id, int *sm_count,
+                                    char *name, int name_len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XPA_OPERATOR_API_H_ */

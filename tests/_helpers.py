@@ -1,0 +1,57 @@
+"""Shared test helpers: run the CUDA path and the oracle on the same seeded inputs."""
+from __future__ import annotations
+
+import numpy as np
+
+from oracle import oracle as O
+from xllms_b200 import workloads as W
+
+# north_star tolerance: 1e-3 relative error for fp32/fp16 KV with fp32
+# accumulation, element-wise |x - ref| <= RTOL * max(|ref|, eps), where
+# eps = 1e-2 * rms(ref) keeps elements that are ~0 in the reference from
+# turning rounding noise into an unbounded relative error.
+RTOL = 1e-3
+
+
+def oracle_out(batch: W.PagedBatch, q, k, v, num_blocks=-1) -> np.ndarray:
+    return O.attention(q, k, v, batch.block_tables, batch.seq_lens, batch.num_kv_heads,
+                       batch.scale, block_size=batch.block_size, num_blocks=num_blocks)
+
+
+def to_device(batch: W.PagedBatch, q, k, v, dev):
+    import torch
+    qt = torch.from_numpy(q).to(dev)
+    kt = torch.from_numpy(k).to(dev)
+    vt = torch.from_numpy(v).to(dev)
+    bt, sl = batch.tables_torch(dev)
+    return qt, kt, vt, bt, sl
+
+
+def check_close(out, ref, rtol=RTOL, what=""):
+    x = out.float().cpu().numpy() if hasattr(out, "cpu") else np.asarray(out)
+    ok, worst = O.rel_err_ok(x, ref, rtol)
+    assert ok, f"{what}: worst |x-ref|/(rtol*max(|ref|,eps)) = {worst:.3f}"
+    return worst
+
+
+def gather_subset(batch: W.PagedBatch, seqs, q_t, k_t, v_t):
+    """Copies the pages of the chosen sequences off the device and relabels the
+    block tables, so the oracle can check a few sequences of a full-size batch."""
+    import torch
+    rows = []
+    pages = []
+    for b in seqs:
+        npg = int(batch.pages_per_seq()[b])
+        ids = batch.block_tables[b, :npg]
+        rows.append(np.arange(len(pages), len(pages) + npg, dtype=np.int32))
+        pages.extend(int(x) for x in ids)
+    idx = torch.tensor(pages, dtype=torch.long, device=k_t.device)
+    k = k_t.index_select(0, idx).cpu().numpy()
+    v = v_t.index_select(0, idx).cpu().numpy()
+    q = q_t[list(seqs)].cpu().numpy()
+    mb = max(len(r) for r in rows)
+    bt = np.full((len(seqs), max(1, mb)), -1, dtype=np.int32)
+    for i, r in enumerate(rows):
+        bt[i, :len(r)] = r
+    sl = batch.seq_lens[list(seqs)].astype(np.int32)
+    return q, k, v, bt, sl

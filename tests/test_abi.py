@@ -1,0 +1,143 @@
+"""The C-ABI boundary without a GPU: libraries load, every declared symbol is
+exported with C linkage, argument checks and the plugin's NULL contract."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from xllms_b200 import _native
+from xllms_b200 import operator_api as PA
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+INCLUDE = os.path.join(ROOT, "include")
+DECL = re.compile(r"^\s*(?:void|int|size_t|const\s+char)\s*\*?\s*(nxt_\w+)\s*\(", re.M)
+
+
+def declared(header):
+    with open(os.path.join(INCLUDE, header)) as f:
+        return sorted(set(DECL.findall(f.read())))
+
+
+def test_every_operator_symbol_exported():
+    names = declared("operator_api.h")
+    assert "nxt_paged_attention" in names and "nxt_paged_attention_v2" in names
+    lib = _native.xpa()
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _native.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_every_plugin_symbol_exported():
+    names = declared("cuda_backend.h")
+    assert names == ["nxt_backend_fini", "nxt_backend_init", "nxt_backend_run"]
+    lib = _native.plugin()
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_plain_c_caller_links_unmangled_symbols(tmp_path):
+    """The reference's own CUDA build exports a C++-mangled nxt_paged_attention
+    that C callers cannot link. Here a C11 program includes the headers, links
+    libxpa.so and makes the reference's zero-size call (tests/test_attention.c:80-100)."""
+    src = tmp_path / "caller.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include "operator_api.h"
+#include "cuda_backend.h"
+int main(void) {
+    int bt = 0, sl = 0;
+    nxt_paged_attention(NULL, NULL, NULL, NULL, &bt, &sl, 0, 0, 0, 0, 0.0f, 0, 0, 0, 0, 0, NULL);
+    nxt_paged_attention_v2(NULL, NULL, NULL, NULL, &bt, &sl, 0, 0, 0, 0, 0.0f, 0, 0, 0, 0, 0, NULL);
+    nxt_paged_attention_flash(NULL, NULL, NULL, NULL, &bt, &sl, 0, 0, 0, 0, 0.0f, 0, 0, 0, 0, 0, NULL);
+    if (nxt_paged_attention_last_error() != NXT_PA_OK) return 1;
+    if (nxt_backend_init(NULL) != -1 || nxt_backend_run(NULL, NULL, NULL) != -1 ||
+        nxt_backend_fini(NULL) != -1) return 2;
+    printf("ok\n");
+    return 0;
+}
+''')
+    exe = tmp_path / "caller"
+    cc = "/usr/bin/gcc" if os.path.exists("/usr/bin/gcc") else "gcc"
+    subprocess.run([cc, "-std=c11", "-Wall", "-Werror", "-I", INCLUDE, str(src), "-o", str(exe),
+                    "-L", _native.LIB_DIR, "-lxllm_cuda_backend", "-lxpa",
+                    f"-Wl,-rpath,{_native.LIB_DIR}"], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr
+
+
+def test_zero_size_call_is_a_noop():
+    PA.nxt_paged_attention(None, None, None, None, None, None, 0, 0, 0, 0, 0.0, 0, 0, 0, 0, 0)
+    assert _native.xpa().nxt_paged_attention_last_error() == _native.NXT_PA_OK
+
+
+@pytest.mark.parametrize("bad", [
+    dict(num_heads=6, num_kv_heads=4),      # heads not a multiple of KV heads
+    dict(dtype_size=3),
+    dict(head_size=0),
+    dict(head_size=512),
+    dict(block_size=0),
+    dict(num_seqs=-1),
+    dict(out=None),
+])
+def test_invalid_arguments_rejected_before_any_launch(bad):
+    args = dict(out=16, query=16, key_cache=16, value_cache=16, block_tables=16, seq_lens=16,
+                num_seqs=1, num_heads=8, head_size=64, num_kv_heads=2, scale=0.125,
+                max_num_blocks_per_seq=1, block_size=16, dtype_size=2,
+                kv_block_stride=2 * 16 * 64, kv_head_stride=16 * 64)
+    args.update(bad)
+    with pytest.raises(PA.PagedAttentionError) as ei:
+        PA.nxt_paged_attention(**args)
+    assert ei.value.code == _native.NXT_PA_EINVAL
+
+
+def test_strerror():
+    for code in (0, -22, -12, -28, -5, 77):
+        assert _native.strerror(code)
+
+
+def test_plugin_null_contract_without_gpu():
+    lib = _native.plugin()
+    assert lib.nxt_backend_init(None) == -1
+    assert lib.nxt_backend_run(None, None, None) == -1
+    assert lib.nxt_backend_fini(None) == -1
+    be = PA.NxtBackend()
+    assert lib.nxt_backend_run(ctypes.byref(be), ctypes.byref(PA.NxtPagedAttentionInput()),
+                               ctypes.c_void_p(16)) == -1       # no backend state yet
+    be.state = PA.NXT_BACKEND_STATE_READY
+    assert lib.nxt_backend_fini(ctypes.byref(be)) == 0
+    assert be.state == PA.NXT_BACKEND_STATE_UNINITIALIZED and not be.backend_state
+
+
+def test_descriptor_layouts_match_reference_abi():
+    # offsets pinned by the reference's tests/mock_cuda_backend.c:22-37 (x86-64)
+    assert PA.NxtBackend.state.offset == 88
+    assert PA.NxtBackend.backend_state.offset == 112
+    assert ctypes.sizeof(PA.NxtBackend) == 120
+    # NxtPagedAttentionInput (backends/cuda_backend.h:29-46): 5 pointers, 10 scalars, stream
+    assert PA.NxtPagedAttentionInput.num_seqs.offset == 40
+    assert PA.NxtPagedAttentionInput.scale.offset == 56
+    assert PA.NxtPagedAttentionInput.stream.offset == 80
+    assert ctypes.sizeof(PA.NxtPagedAttentionInput) == 88
+
+
+def test_layout_offsets_in_c(tmp_path):
+    src = tmp_path / "off.c"
+    src.write_text(r'''
+#include <stddef.h>
+#include <stdio.h>
+#include "cuda_backend.h"
+#include "xllm_backend_abi.h"
+int main(void) {
+    printf("%zu %zu %zu %zu %zu\n", offsetof(struct NxtBackend, state),
+           offsetof(struct NxtBackend, backend_state), sizeof(struct NxtBackend),
+           offsetof(NxtPagedAttentionInput, stream), sizeof(NxtPagedAttentionInput));
+    return 0;
+}
+''')
+    exe = tmp_path / "off"
+    cc = "/usr/bin/gcc" if os.path.exists("/usr/bin/gcc") else "gcc"
+    subprocess.run([cc, "-std=c11", "-I", INCLUDE, str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
+    assert out == ["88", "112", "120", "80", "88"]

@@ -1,0 +1,263 @@
+"""Parity of the CUDA kernels (through the C ABI) with the CPU oracle."""
+import numpy as np
+import pytest
+
+from _helpers import RTOL, check_close, gather_subset, oracle_out, to_device
+from oracle import oracle as O
+from xllms_b200 import _native
+from xllms_b200 import operator_api as PA
+from xllms_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+EDGE_LENS = [0, 1, 15, 16, 17, 511, 512, 513, 1000]
+
+
+def _run_dropin(entry, batch, qt, kt, vt, bt, sl, out):
+    getattr(PA, entry)(out, qt, kt, vt, bt, sl, batch.num_seqs, batch.num_heads,
+                       batch.head_size, batch.num_kv_heads, batch.scale, batch.max_blocks,
+                       batch.block_size, batch.dtype_size, batch.kv_block_stride,
+                       batch.kv_head_stride, None)
+
+
+@pytest.mark.parametrize("entry", ["nxt_paged_attention", "nxt_paged_attention_v2",
+                                   "nxt_paged_attention_flash"])
+def test_config1_dropin_entries(cuda, entry):
+    import torch
+    b = W.config1()
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = torch.full_like(qt, float("nan"))
+    _run_dropin(entry, b, qt, kt, vt, bt, sl, out)
+    torch.cuda.synchronize()
+    check_close(out, ref, what=entry)
+    assert PA.device_status() == 0
+
+
+@pytest.mark.parametrize("group", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("head_size", [64, 128, 256])
+def test_fp16_groups_and_heads(cuda, group, head_size):
+    hkv = 2
+    b = W.make_batch("g", EDGE_LENS, hkv * group, hkv, head_size, "f16", 100 + group,
+                     value_std=0.5)
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = PA.paged_attention(qt, kt, vt, bt, sl)
+    check_close(out, ref, what=f"GS={group} D={head_size}")
+    expect = _native.NXT_PA_PATH_TMA_MMA if not (group > 8 and head_size == 256) \
+        else _native.NXT_PA_PATH_GENERIC
+    assert PA.kernel_path(kt, vt, b.num_heads, head_size, hkv, 16, 2, b.kv_block_stride,
+                          b.kv_head_stride) == expect
+    assert PA.device_status() == 0
+
+
+@pytest.mark.parametrize("head_size", [32, 64, 80, 96, 112, 128, 192, 256])
+@pytest.mark.parametrize("dtype", ["f16", "f32"])
+def test_all_reference_head_sizes(cuda, head_size, dtype):
+    # The reference dispatches head sizes 32..256 (include/operator_api.h:40-41).
+    b = W.make_batch("h", [5, 33, 300], 8, 4, head_size, dtype, 7 + head_size)
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = PA.paged_attention(qt, kt, vt, bt, sl)
+    check_close(out, ref, what=f"{dtype} D={head_size}")
+
+
+@pytest.mark.parametrize("block_size", [8, 32])
+def test_other_page_sizes(cuda, block_size):
+    b = W.make_batch("p", [1, 31, 32, 33, 700], 8, 2, 128, "f16", 17, block_size=block_size)
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = PA.paged_attention(qt, kt, vt, bt, sl)
+    check_close(out, ref, what=f"block_size={block_size}")
+
+
+@pytest.mark.parametrize("lens", [[4096], [20000, 3, 513], [131072 // 8] * 2])
+def test_split_context(cuda, lens):
+    b = W.make_batch("s", lens, 16, 2, 128, "f16", 23)
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = PA.paged_attention(qt, kt, vt, bt, sl)
+    check_close(out, ref, what=f"split {lens}")
+
+
+def test_prefix_shared_tables(cuda):
+    b = W.config4(num_seqs=16)
+    assert b.kv_bytes_unique() < b.kv_bytes()
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = PA.paged_attention(qt, kt, vt, bt, sl)
+    check_close(out, ref, what="prefix shared")
+
+
+def test_zero_inputs_give_zero_output(cuda):
+    # The one numerical result the reference's own tests pin:
+    # all-zero inputs give an all-zero output (tests/test_attention_bench.c:387-389).
+    import torch
+    b = W.make_batch("z", [32], 4, 2, 64, "f16", 1)
+    qt = torch.zeros((1, 4, 64), dtype=torch.float16, device=cuda)
+    kt = torch.zeros((b.num_blocks, 2, 16, 64), dtype=torch.float16, device=cuda)
+    bt, sl = b.tables_torch(cuda)
+    out = PA.paged_attention(qt, kt, kt.clone(), bt, sl)
+    assert float(out.abs().max()) < 1e-3
+
+
+def test_uniform_weights_give_mean_of_values(cuda):
+    # Q = 0 makes every weight 1/L: the output is the mean of the visited V rows.
+    import torch
+    b = W.make_batch("u", [1, 17, 100, 600], 8, 2, 128, "f16", 3)
+    q, k, v = b.values_numpy()
+    q[:] = 0
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = PA.paged_attention(qt, kt, vt, bt, sl).float().cpu().numpy()
+    vv = v.astype(np.float64)
+    for i in range(b.num_seqs):
+        L = int(b.seq_lens[i])
+        rows = [vv[b.block_tables[i, t // 16], :, t % 16, :] for t in range(L)]
+        mean = np.mean(rows, axis=0)  # [Hkv, D]
+        expect = np.repeat(mean, 4, axis=0)
+        assert np.allclose(out[i], expect, rtol=2e-3, atol=2e-3)
+
+
+def test_single_hot_key_selects_its_value(cuda):
+    import torch
+    b = W.make_batch("hot", [300], 4, 1, 64, "f16", 9)
+    q, k, v = b.values_numpy()
+    k[:] = 0
+    q[:] = 1
+    hot = 123
+    page, slot = b.block_tables[0, hot // 16], hot % 16
+    k[page, 0, slot, :] = 2.0  # score 2*64*0.125 = 16 nats above the rest
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = PA.paged_attention(qt, kt, vt, bt, sl).float().cpu().numpy()
+    ref = oracle_out(b, q, k, v)
+    check_close(out, ref, what="hot key")
+    assert np.allclose(out[0, 0], v[page, 0, slot].astype(np.float32), atol=1e-3 * 8)
+
+
+def test_masked_pages_and_status(cuda):
+    import torch
+    b = W.make_batch("m", [200, 64], 8, 2, 128, "f16", 31)
+    b.block_tables[0, 3] = -1          # a hole inside sequence 0
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    PA.device_status(clear=True)
+    out = PA.paged_attention(qt, kt, vt, bt, sl)
+    check_close(out, ref, what="masked page")
+    assert PA.device_status() & _native.NXT_PA_DEV_BAD_PAGE
+
+
+def test_out_of_range_pages_masked_with_num_blocks(cuda):
+    b = W.make_batch("r", [100, 90], 8, 2, 128, "f16", 37)
+    q, k, v = b.values_numpy()
+    limit = int(b.block_tables[0, 2])  # every page id >= limit is out of range
+    ref = oracle_out(b, q, k, v, num_blocks=limit)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    PA.device_status(clear=True)
+    out = PA.paged_attention(qt, kt, vt, bt, sl, num_blocks=limit)
+    check_close(out, ref, what="num_blocks mask")
+    assert PA.device_status() & _native.NXT_PA_DEV_BAD_PAGE
+
+
+def test_seq_len_clamped_to_table(cuda):
+    import torch
+    b = W.make_batch("c", [64, 40], 4, 2, 64, "f16", 41, max_blocks=4)
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    sl_long = sl.clone()
+    sl_long[0] = 10_000                 # beyond max_blocks * block_size = 64
+    PA.device_status(clear=True)
+    out = PA.paged_attention(qt, kt, vt, bt, sl_long)
+    check_close(out, ref, what="clamp")
+    assert PA.device_status() & _native.NXT_PA_DEV_SEQ_CLAMPED
+
+
+def test_nan_garbage_past_seq_len_is_ignored(cuda):
+    import torch
+    b = W.make_batch("n", [20, 5], 8, 2, 128, "f16", 43)
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    for i in range(b.num_seqs):
+        L = int(b.seq_lens[i])
+        last = b.block_tables[i, (L - 1) // 16]
+        k[last, :, L % 16:, :] = np.inf
+        v[last, :, L % 16:, :] = np.nan
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = PA.paged_attention(qt, kt, vt, bt, sl)
+    check_close(out, ref, what="garbage tail")
+
+
+def test_caller_workspace_and_stream(cuda):
+    import torch
+    b = W.make_batch("w", [3000, 70], 8, 2, 128, "f16", 47)
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    need = PA.workspace_size(b.num_seqs, b.num_heads, 128, 2, b.max_blocks)
+    assert need > 0
+    small = torch.empty(need // 2, dtype=torch.uint8, device=cuda)
+    with pytest.raises(PA.PagedAttentionError) as ei:
+        PA.paged_attention(qt, kt, vt, bt, sl, workspace=small)
+    assert ei.value.code == _native.NXT_PA_EWORKSPACE
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        out = PA.paged_attention(qt, kt, vt, bt, sl, workspace=ws, device_status=status, stream=s)
+    s.synchronize()
+    check_close(out, ref, what="caller workspace")
+    assert int(status.item()) == 0
+
+
+def test_repeatable_bitwise(cuda):
+    b = W.make_batch("d", [777, 4000], 32, 8, 128, "f16", 53)
+    q, k, v = b.values_numpy()
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    a = PA.paged_attention(qt, kt, vt, bt, sl)
+    c = PA.paged_attention(qt, kt, vt, bt, sl)
+    assert bool((a == c).all())
+
+
+def test_invalid_arguments_launch_nothing(cuda):
+    import torch
+    b = W.make_batch("i", [16], 6, 4, 64, "f16", 1)  # 6 % 4 != 0 after construction
+    q, k, v = b.values_numpy()
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = torch.zeros_like(qt)
+    with pytest.raises(PA.PagedAttentionError) as ei:
+        PA.nxt_paged_attention(out, qt, kt, vt, bt, sl, 1, 6, 64, 4, 0.125, 1, 16, 2,
+                               4 * 16 * 64, 16 * 64)
+    assert ei.value.code == _native.NXT_PA_EINVAL
+    with pytest.raises(PA.PagedAttentionError):
+        PA.nxt_paged_attention(out, qt, kt, vt, bt, sl, 1, 4, 64, 4, 0.125, 1, 16, 3,
+                               4 * 16 * 64, 16 * 64)
+    assert float(out.abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("cfg", ["c2", "c3", "c4"])
+def test_full_size_configs_sampled(cuda, cfg):
+    """Full BASELINE sizes on the device; a sample of sequences is re-checked
+    by the oracle from the device's own pages."""
+    import torch
+    b = W.CONFIGS[cfg]()
+    qt, kt, vt = b.values_torch(cuda)
+    bt, sl = b.tables_torch(cuda)
+    out = PA.paged_attention(qt, kt, vt, bt, sl)
+    torch.cuda.synchronize()
+    assert PA.device_status() == 0
+    lens = b.seq_lens
+    picks = {int(np.argmin(lens)), int(np.argmax(lens))}
+    if cfg != "c3":
+        picks |= {0, b.num_seqs - 1}
+    picks = sorted(picks)
+    q, k, v, sbt, ssl = gather_subset(b, picks, qt, kt, vt)
+    ref = O.attention(q, k, v, sbt, ssl, b.num_kv_heads, b.scale, threads=0)
+    check_close(out[picks], ref, what=cfg)
+    assert torch.isfinite(out).all()

@@ -1,0 +1,410 @@
+// pa_api.cu — the C ABI of libxpa.so (include/operator_api.h): argument
+// checks, launch planning, tensor-map encoding, library-owned workspaces and
+// status words, and the drop-in entry points.
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "operator_api.h"
+#include "pa_launch.h"
+
+namespace {
+
+thread_local int g_last_error = NXT_PA_OK;
+thread_local cudaEvent_t g_prof_before = nullptr;  // one-shot timing events
+thread_local cudaEvent_t g_prof_after = nullptr;
+
+constexpr unsigned long long kWaitBudgetNs = 1000000000ull;  // 1 s per pipeline wait
+constexpr int kMaxDevices = 64;
+
+std::mutex g_mu;
+
+struct DeviceState {
+  bool probed = false;
+  int sm_count = 0;
+  int* status = nullptr;  // library status word
+};
+DeviceState g_dev[kMaxDevices];
+
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+// Keyed by (device, stream) so calls on different streams never share partials.
+std::map<std::pair<int, uintptr_t>, Workspace> g_ws;
+
+int map_cuda(cudaError_t e) { return e == cudaSuccess ? NXT_PA_OK : NXT_PA_ECUDA; }
+
+int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
+
+// Per-device facts; status word allocated on first use. Caller holds g_mu.
+int device_state_locked(int dev, DeviceState** out) {
+  if (dev < 0 || dev >= kMaxDevices) return NXT_PA_EINVAL;
+  DeviceState& d = g_dev[dev];
+  if (!d.probed) {
+    int sms = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return NXT_PA_ECUDA;
+    d.sm_count = sms;
+    d.probed = true;
+  }
+  if (!d.status) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, 256) != cudaSuccess) return NXT_PA_ENOMEM;
+    if (cudaMemset(p, 0, 256) != cudaSuccess) {
+      cudaFree(p);
+      return NXT_PA_ECUDA;
+    }
+    d.status = static_cast<int*>(p);
+  }
+  *out = &d;
+  return NXT_PA_OK;
+}
+
+int sm_count_of(int dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  DeviceState& d = g_dev[dev];
+  if (!d.probed) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return 148;
+    d.sm_count = sms;
+    d.probed = true;
+  }
+  return d.sm_count;
+}
+
+struct Plan {
+  int part_pages = 32;
+  int max_parts = 1;
+  size_t ws_bytes = 0;
+};
+
+// Partition size: 32 pages (512 tokens at page size 16) by default, halved
+// while the grid would leave the GPU short of work, and doubled while the
+// reduce kernel's per-row weight table would not fit its shared memory.
+Plan make_plan(int B, int Hq, int D, int Hkv, int max_blocks, int nsm) {
+  Plan pl;
+  const long long mb = max_blocks > 0 ? max_blocks : 1;
+  int pp = 32;
+  while (pp > 4 && (long long)B * Hkv * ceil_div(mb, pp) < 12LL * nsm) pp >>= 1;
+  while (ceil_div(mb, pp) > 8192) pp <<= 1;
+  pl.part_pages = pp;
+  pl.max_parts = ceil_div(mb, pp);
+  if (pl.max_parts > 1)
+    pl.ws_bytes = (size_t)B * Hq * pl.max_parts * (size_t)(D + 2) * sizeof(float);
+  return pl;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// One pool (K or V) as a 4-D fp16 tensor {d, slot, kv head, page}, boxed
+// 64 x 16 x 1 x 1 with 128-byte swizzle. An unknown pool size uses the
+// largest page coordinate TMA accepts.
+bool encode_pool(CUtensorMap* m, const void* base, int D, int Hkv, long long num_blocks,
+                 long long kbs, long long khs) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, 16u, (cuuint64_t)Hkv,
+                        (cuuint64_t)(num_blocks > 0 ? num_blocks : (long long)INT_MAX)};
+  cuuint64_t strides[3] = {(cuuint64_t)D * 2u, (cuuint64_t)khs * 2u, (cuuint64_t)kbs * 2u};
+  cuuint32_t box[4] = {64u, 16u, 1u, 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool fast_layout_ok(const void* k, const void* v, int D, int Hkv, long long kbs, long long khs) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(k), b = reinterpret_cast<uintptr_t>(v);
+  if ((a | b) & 15u) return false;
+  if ((kbs * 2) % 16 || (khs * 2) % 16) return false;
+  if (khs < 16LL * D) return false;             // a page's slots are contiguous rows
+  if (Hkv > 1 && kbs < khs * Hkv && khs != 0) {
+    // Non-standard order (heads outermost): tensor-map strides may then not
+    // be increasing; leave such pools to the generic kernel.
+    return false;
+  }
+  return true;
+}
+
+int check_args(const void* out, const void* q, const void* k, const void* v, const int* bt,
+               const int* sl, int B, int Hq, int D, int Hkv, int max_blocks, int bs, int ds,
+               long long kbs, long long khs) {
+  if (B < 0) return NXT_PA_EINVAL;
+  if (B == 0) return NXT_PA_OK;
+  if (!out || !q || !k || !v || !bt || !sl) return NXT_PA_EINVAL;
+  if (Hq <= 0 || Hkv <= 0 || Hq % Hkv) return NXT_PA_EINVAL;
+  if (D <= 0 || D > 256) return NXT_PA_EINVAL;
+  if (ds != 2 && ds != 4) return NXT_PA_EINVAL;
+  if (bs <= 0 || max_blocks < 0) return NXT_PA_EINVAL;
+  if (kbs < 0 || khs < 0) return NXT_PA_EINVAL;
+  return NXT_PA_OK;
+}
+
+int run(void* out, const void* q, const void* k, const void* v, const int* bt, const int* sl,
+        int B, int Hq, int D, int Hkv, float scale, int max_blocks, int bs, int ds,
+        long long kbs, long long khs, long long num_blocks, void* ws, size_t ws_bytes,
+        int* dev_status, cudaStream_t st) {
+  int rc = check_args(out, q, k, v, bt, sl, B, Hq, D, Hkv, max_blocks, bs, ds, kbs, khs);
+  if (rc != NXT_PA_OK || B == 0) return rc;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NXT_PA_ECUDA;
+  const Plan pl = make_plan(B, Hq, D, Hkv, max_blocks, sm_count_of(dev));
+  if ((long long)B * Hkv * pl.max_parts > INT_MAX || (long long)B * Hq > INT_MAX)
+    return NXT_PA_EINVAL;
+
+  int* status = dev_status;
+  void* part = ws;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!status) {
+      DeviceState* d = nullptr;
+      rc = device_state_locked(dev, &d);
+      if (rc != NXT_PA_OK) return rc;
+      status = d->status;
+    }
+    if (pl.ws_bytes > 0) {
+      if (ws) {
+        if (ws_bytes < pl.ws_bytes) return NXT_PA_EWORKSPACE;
+      } else {
+        Workspace& w = g_ws[{dev, reinterpret_cast<uintptr_t>(st)}];
+        if (w.bytes < pl.ws_bytes) {
+          if (w.ptr) cudaFree(w.ptr);  // synchronises: no kernel still reads it
+          w.ptr = nullptr;
+          w.bytes = 0;
+          if (cudaMalloc(&w.ptr, pl.ws_bytes) != cudaSuccess) return NXT_PA_ENOMEM;
+          w.bytes = pl.ws_bytes;
+        }
+        part = w.ptr;
+      }
+    }
+  }
+
+  xpa::Params p{};
+  p.out = out;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.block_tables = bt;
+  p.seq_lens = sl;
+  p.part_o = static_cast<float*>(part);
+  p.part_ml = part ? static_cast<float*>(part) + (size_t)B * Hq * pl.max_parts * D : nullptr;
+  p.status = status;
+  p.kv_block_stride = kbs;
+  p.kv_head_stride = khs;
+  p.num_blocks = num_blocks;
+  p.timeout_ns = kWaitBudgetNs;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.D = D;
+  p.GS = Hq / Hkv;
+  p.max_blocks = max_blocks;
+  p.block_size = bs;
+  p.part_pages = pl.part_pages;
+  p.max_parts = pl.max_parts;
+  p.scale_log2 = scale * 1.4426950408889634f;
+
+  cudaError_t e;
+  CUtensorMap tk, tv;
+  const bool fast = xpa::fast_path_shape_ok(D, p.GS, bs, ds) &&
+                    fast_layout_ok(k, v, D, Hkv, kbs, khs) &&
+                    (reinterpret_cast<uintptr_t>(q) & 3u) == 0 &&
+                    encode_pool(&tk, k, D, Hkv, num_blocks, kbs, khs) &&
+                    encode_pool(&tv, v, D, Hkv, num_blocks, kbs, khs);
+  cudaEvent_t ev_a = g_prof_before, ev_b = g_prof_after;
+  g_prof_before = g_prof_after = nullptr;
+  if (ev_a && cudaEventRecord(ev_a, st) != cudaSuccess) return NXT_PA_ECUDA;
+  e = fast ? xpa::launch_fast(tk, tv, p, st) : xpa::launch_generic(p, ds, st);
+  if (e != cudaSuccess) return map_cuda(e);
+  if (ev_b && cudaEventRecord(ev_b, st) != cudaSuccess) return NXT_PA_ECUDA;
+  if (pl.max_parts > 1) {
+    e = xpa::launch_reduce(p, ds, st);
+    if (e != cudaSuccess) return map_cuda(e);
+  }
+  return NXT_PA_OK;
+}
+
+void dropin(void* out, const void* q, const void* k, const void* v, const int* bt, const int* sl,
+            int B, int Hq, int D, int Hkv, float scale, int max_blocks, int bs, int ds, int kbs,
+            int khs, nxt_stream_t stream) {
+  g_last_error = run(out, q, k, v, bt, sl, B, Hq, D, Hkv, scale, max_blocks, bs, ds, kbs, khs,
+                     -1, nullptr, 0, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+void nxt_paged_attention(void* out, const void* query, const void* key_cache,
+                         const void* value_cache, const int* block_tables, const int* seq_lens,
+                         int num_seqs, int num_heads, int head_size, int num_kv_heads,
+                         float scale, int max_num_blocks_per_seq, int block_size, int dtype_size,
+                         int kv_block_stride, int kv_head_stride, nxt_stream_t stream) {
+  dropin(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads,
+         head_size, num_kv_heads, scale, max_num_blocks_per_seq, block_size, dtype_size,
+         kv_block_stride, kv_head_stride, stream);
+}
+
+void nxt_paged_attention_v2(void* out, const void* query, const void* key_cache,
+                            const void* value_cache, const int* block_tables,
+                            const int* seq_lens, int num_seqs, int num_heads, int head_size,
+                            int num_kv_heads, float scale, int max_num_blocks_per_seq,
+                            int block_size, int dtype_size, int kv_block_stride,
+                            int kv_head_stride, nxt_stream_t stream) {
+  dropin(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads,
+         head_size, num_kv_heads, scale, max_num_blocks_per_seq, block_size, dtype_size,
+         kv_block_stride, kv_head_stride, stream);
+}
+
+void nxt_paged_attention_flash(void* out, const void* query, const void* key_cache,
+                               const void* value_cache, const int* block_tables,
+                               const int* seq_lens, int num_seqs, int num_heads, int head_size,
+                               int num_kv_heads, float scale, int max_num_blocks_per_seq,
+                               int block_size, int dtype_size, int kv_block_stride,
+                               int kv_head_stride, nxt_stream_t stream) {
+  dropin(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads,
+         head_size, num_kv_heads, scale, max_num_blocks_per_seq, block_size, dtype_size,
+         kv_block_stride, kv_head_stride, stream);
+}
+
+int nxt_paged_attention_last_error(void) { return g_last_error; }
+
+const char* nxt_paged_attention_strerror(int code) {
+  switch (code) {
+    case NXT_PA_OK: return "ok";
+    case NXT_PA_EINVAL: return "unsupported or inconsistent arguments";
+    case NXT_PA_ENOMEM: return "workspace allocation failed";
+    case NXT_PA_EWORKSPACE: return "workspace smaller than required";
+    case NXT_PA_ECUDA: return "CUDA call failed";
+    default: return "unknown status";
+  }
+}
+
+int nxt_paged_attention_ex(void* out, const void* query, const void* key_cache,
+                           const void* value_cache, const int* block_tables, const int* seq_lens,
+                           int num_seqs, int num_heads, int head_size, int num_kv_heads,
+                           float scale, int max_num_blocks_per_seq, int block_size,
+                           int dtype_size, int64_t kv_block_stride, int64_t kv_head_stride,
+                           int64_t num_blocks, void* workspace, size_t workspace_bytes,
+                           int* device_status, nxt_stream_t stream) {
+  return run(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads,
+             head_size, num_kv_heads, scale, max_num_blocks_per_seq, block_size, dtype_size,
+             kv_block_stride, kv_head_stride, num_blocks, workspace, workspace_bytes,
+             device_status, static_cast<cudaStream_t>(stream));
+}
+
+size_t nxt_paged_attention_workspace_size(int num_seqs, int num_heads, int head_size,
+                                          int num_kv_heads, int max_num_blocks_per_seq,
+                                          int block_size, int dtype_size) {
+  (void)block_size;
+  (void)dtype_size;
+  if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0 || head_size <= 0) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  return make_plan(num_seqs, num_heads, head_size, num_kv_heads, max_num_blocks_per_seq,
+                   sm_count_of(dev))
+      .ws_bytes;
+}
+
+int nxt_paged_attention_path(const void* key_cache, const void* value_cache, int num_heads,
+                             int head_size, int num_kv_heads, int block_size, int dtype_size,
+                             int64_t kv_block_stride, int64_t kv_head_stride) {
+  if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || head_size <= 0 ||
+      head_size > 256 || (dtype_size != 2 && dtype_size != 4) || block_size <= 0)
+    return NXT_PA_PATH_NONE;
+  CUtensorMap tk, tv;
+  if (xpa::fast_path_shape_ok(head_size, num_heads / num_kv_heads, block_size, dtype_size) &&
+      fast_layout_ok(key_cache, value_cache, head_size, num_kv_heads, kv_block_stride,
+                     kv_head_stride) &&
+      encode_pool(&tk, key_cache, head_size, num_kv_heads, -1, kv_block_stride,
+                  kv_head_stride) &&
+      encode_pool(&tv, value_cache, head_size, num_kv_heads, -1, kv_block_stride,
+                  kv_head_stride))
+    return NXT_PA_PATH_TMA_MMA;
+  return NXT_PA_PATH_GENERIC;
+}
+
+int nxt_paged_attention_device_status(int clear) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NXT_PA_ECUDA;
+  int* st = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState* d = nullptr;
+    int rc = device_state_locked(dev, &d);
+    if (rc != NXT_PA_OK) return rc;
+    st = d->status;
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) return NXT_PA_ECUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, st, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return NXT_PA_ECUDA;
+  if (clear && cudaMemset(st, 0, sizeof(int)) != cudaSuccess) return NXT_PA_ECUDA;
+  if (clear && cudaDeviceSynchronize() != cudaSuccess) return NXT_PA_ECUDA;
+  return v;
+}
+
+int nxt_paged_attention_release_workspaces(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  int prev = 0;
+  const bool have_prev = cudaGetDevice(&prev) == cudaSuccess;
+  int rc = NXT_PA_OK;
+  for (auto& kv : g_ws) {
+    if (!kv.second.ptr) continue;
+    if (cudaSetDevice(kv.first.first) != cudaSuccess || cudaFree(kv.second.ptr) != cudaSuccess)
+      rc = NXT_PA_ECUDA;
+  }
+  g_ws.clear();
+  for (int dev = 0; dev < kMaxDevices; ++dev) {
+    if (!g_dev[dev].status) continue;
+    if (cudaSetDevice(dev) != cudaSuccess || cudaFree(g_dev[dev].status) != cudaSuccess)
+      rc = NXT_PA_ECUDA;
+    g_dev[dev].status = nullptr;
+  }
+  if (have_prev) cudaSetDevice(prev);
+  return rc;
+}
+
+int nxt_paged_attention_profile_next(void* before, void* after) {
+  g_prof_before = static_cast<cudaEvent_t>(before);
+  g_prof_after = static_cast<cudaEvent_t>(after);
+  return NXT_PA_OK;
+}
+
+int nxt_paged_attention_device_info(int* device_id, int* sm_count, char* name, int name_len) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NXT_PA_ECUDA;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return NXT_PA_ECUDA;
+  if (device_id) *device_id = dev;
+  if (sm_count) *sm_count = prop.multiProcessorCount;
+  if (name && name_len > 0) {
+    std::strncpy(name, prop.name, (size_t)name_len - 1);
+    name[name_len - 1] = '\0';
+  }
+  return NXT_PA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,227 @@
+// pa_device.cuh — sm_100a device primitives and the shared kernel parameter
+// block for paged decode attention. Inline PTX only; no library kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace xpa {
+
+// Device status bits; the same values as NXT_PA_DEV_* in operator_api.h.
+constexpr int kDevTimeout = 0x1;
+constexpr int kDevBadPage = 0x2;
+constexpr int kDevSeqClamped = 0x4;
+
+// Everything a launch needs besides the tensor maps. Strides are in elements.
+struct Params {
+  void* out;              // [B][Hq][D]
+  const void* q;          // [B][Hq][D]
+  const void* k;          // paged pool
+  const void* v;          // paged pool
+  const int* block_tables;  // [B][max_blocks]
+  const int* seq_lens;      // [B]
+  float* part_o;   // [B][Hq][max_parts][D] unnormalised partial outputs
+  float* part_ml;  // [B][Hq][max_parts][2] (max in log2 units, sum of exp2)
+  int* status;     // device status word (NXT_PA_DEV_* bits), may be null
+  long long kv_block_stride;
+  long long kv_head_stride;
+  long long num_blocks;  // <= 0: unknown, no upper bound check
+  unsigned long long timeout_ns;  // bound on every pipeline wait
+  int B, Hq, Hkv, D, GS;
+  int max_blocks, block_size;
+  int part_pages, max_parts;
+  float scale_log2;  // scale * log2(e): scores live in the exp2 domain
+};
+
+// One unit of work: context partition `part` of (sequence b, KV head kvh).
+struct Item {
+  int b, kvh, part;
+  int L;            // clamped context length of sequence b
+  int page_begin;   // first page of this partition
+  int page_end;     // one past its last page
+  int nparts;       // partitions of sequence b (0 when L == 0)
+};
+
+enum ItemKind { kItemNone = 0, kItemZero = 1, kItemWork = 2 };
+
+__device__ __forceinline__ void raise_status(const Params& p, int bits) {
+  if (p.status) atomicOr(p.status, bits);
+}
+
+// Grid index -> item. Index order is (b, kvh, part) with part fastest, so the
+// CTAs of one sequence are dispatched together.
+__device__ __forceinline__ ItemKind decode_item(const Params& p, int idx, Item& it) {
+  it.part = idx % p.max_parts;
+  const int rest = idx / p.max_parts;
+  it.kvh = rest % p.Hkv;
+  it.b = rest / p.Hkv;
+  int L = __ldg(p.seq_lens + it.b);
+  const long long cap = (long long)p.max_blocks * p.block_size;
+  if (L < 0 || (long long)L > cap) {
+    if (it.part == 0 && it.kvh == 0 && threadIdx.x == 0) raise_status(p, kDevSeqClamped);
+    L = L < 0 ? 0 : (int)cap;
+  }
+  it.L = L;
+  const int npages = (L + p.block_size - 1) / p.block_size;
+  it.nparts = (npages + p.part_pages - 1) / p.part_pages;
+  if (it.nparts == 0) return it.part == 0 ? kItemZero : kItemNone;
+  if (it.part >= it.nparts) return kItemNone;
+  it.page_begin = it.part * p.part_pages;
+  it.page_end = min(npages, it.page_begin + p.part_pages);
+  return kItemWork;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// 2^x via the PTX approximate instruction (ex2.approx, ftz): 2^-inf = +0.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ── mbarrier ────────────────────────────────────────────────────────────
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok;
+}
+
+// Waits for the phase with the given parity to complete, for at most
+// budget_ns of wall time. Returns false when the budget ran out.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t budget_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0u && globaltimer_ns() - t0 > budget_ns) return false;
+  }
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) accesses of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ── TMA (tensor, tiled, no multicast) ───────────────────────────────────
+__device__ __forceinline__ void tmap_prefetch(const CUtensorMap* tm) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* tm, int c0, int c1,
+                                            int c2, int c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+// ── warp-level tensor-core fragments ────────────────────────────────────
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                              uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D += A(16x16, row) * B(16x8, col), fp16 inputs, fp32 accumulate.
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                              uint32_t a2, uint32_t a3, uint32_t b0,
+                                              uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7},"
+      " {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Transposes an 8x8 b16 matrix held one 32-bit pair per lane.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float2 unpack_half2(uint32_t u) {
+  __half2 h = *reinterpret_cast<__half2*>(&u);
+  return __half22float2(h);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_float(T x);
+template <>
+__device__ __forceinline__ float to_float<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_float<__half>(__half x) { return __half2float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_float(float x);
+template <>
+__device__ __forceinline__ float from_float<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __half from_float<__half>(float x) { return __float2half_rn(x); }
+
+}  // namespace xpa

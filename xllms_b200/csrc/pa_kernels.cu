@@ -1,0 +1,601 @@
+// pa_kernels.cu — paged decode attention kernels for sm_100a.
+//
+// Work decomposition (all kernels): one CTA per item = (sequence b, KV head
+// kvh, context partition part). A partition is `part_pages` consecutive pages
+// of the sequence's block-table row. A sequence that fits in one partition is
+// finished in place (normalised output written directly); longer ones write
+// per-partition partials (running max m, sum l, unnormalised o) that
+// pa_reduce_kernel merges by log-sum-exp. Scores are kept in the exp2 domain
+// (scale * log2 e folded into the score), which is the same softmax.
+//
+// Reference semantics followed: GQA mapping kv = h / (Hq/Hkv)
+// (examples/text_gen.c:1285), max-subtracted softmax and o = sum w*v
+// (examples/text_gen.c:1288-1309), paged indexing
+// phys*kv_block_stride + kvh*kv_head_stride + slot*D + d
+// (operators/page_attention_v2.cu:143-146), zero row for seq_len 0
+// (operators/page_attention.cu:157).
+#include "pa_device.cuh"
+#include "pa_launch.h"
+
+namespace xpa {
+
+// ════════════════════════════════════════════════════════════════════════
+// Generic path: CUDA cores, any head size <= 256, fp16 or fp32, any page size.
+// Each of the 4 warps walks every 4th token of the item; lanes split the head
+// dimension (DPL dims per lane) and each token's K row is used for HG query
+// heads of the group at once, so K/V are read once per HG heads.
+// ════════════════════════════════════════════════════════════════════════
+template <typename T, int DPL, int HG>
+__global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
+  constexpr int NW = 4;
+  constexpr int DMAX = DPL * 32;
+  __shared__ float sm_o[NW][HG][DMAX + 1];
+  __shared__ float sm_m[NW][HG];
+  __shared__ float sm_l[NW][HG];
+
+  Item it;
+  const ItemKind kind = decode_item(p, blockIdx.x, it);
+  if (kind == kItemNone) return;
+  const int D = p.D, GS = p.GS;
+  T* out = static_cast<T*>(p.out);
+  if (kind == kItemZero) {
+    T* dst = out + ((long long)it.b * p.Hq + (long long)it.kvh * GS) * D;
+    for (int e = threadIdx.x; e < GS * D; e += blockDim.x) dst[e] = from_float<T>(0.f);
+    return;
+  }
+
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const T* Q = static_cast<const T*>(p.q);
+  const T* K = static_cast<const T*>(p.k);
+  const T* V = static_cast<const T*>(p.v);
+  const int* bt_row = p.block_tables + (long long)it.b * p.max_blocks;
+  const int t_begin = it.page_begin * p.block_size;
+  const int t_end = min(it.L, it.page_end * p.block_size);
+
+  for (int hg0 = 0; hg0 < GS; hg0 += HG) {
+    const int nh = min(HG, GS - hg0);
+    float q[HG][DPL], o[HG][DPL], m[HG], l[HG];
+#pragma unroll
+    for (int j = 0; j < HG; ++j) {
+      const long long qrow = ((long long)it.b * p.Hq + (long long)it.kvh * GS + hg0 + j) * D;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        const int d = lane + 32 * i;
+        q[j][i] = (j < nh && d < D) ? to_float(Q[qrow + d]) : 0.f;
+        o[j][i] = 0.f;
+      }
+      m[j] = -INFINITY;
+      l[j] = 0.f;
+    }
+
+    for (int t = t_begin + w; t < t_end; t += NW) {
+      const int phys = __ldg(bt_row + t / p.block_size);
+      if (phys < 0 || (p.num_blocks > 0 && phys >= p.num_blocks)) {
+        if (lane == 0 && hg0 == 0) raise_status(p, kDevBadPage);
+        continue;
+      }
+      const long long base = (long long)phys * p.kv_block_stride +
+                             (long long)it.kvh * p.kv_head_stride +
+                             (long long)(t % p.block_size) * D;
+      float kf[DPL], vf[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        const int d = lane + 32 * i;
+        kf[i] = d < D ? to_float(K[base + d]) : 0.f;
+        vf[i] = d < D ? to_float(V[base + d]) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < HG; ++j) {
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) dot = fmaf(q[j][i], kf[i], dot);
+        const float s = warp_sum(dot) * p.scale_log2;
+        const float mn = fmaxf(m[j], s);
+        const float alpha = ex2(m[j] - mn);
+        const float pj = ex2(s - mn);
+        l[j] = fmaf(l[j], alpha, pj);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) o[j][i] = fmaf(o[j][i], alpha, pj * vf[i]);
+        m[j] = mn;
+      }
+    }
+
+#pragma unroll
+    for (int j = 0; j < HG; ++j) {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) sm_o[w][j][lane + 32 * i] = o[j][i];
+      if (lane == 0) {
+        sm_m[w][j] = m[j];
+        sm_l[w][j] = l[j];
+      }
+    }
+    __syncthreads();
+
+    for (int e = threadIdx.x; e < nh * D; e += blockDim.x) {
+      const int j = e / D, d = e - j * D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int ww = 0; ww < NW; ++ww) M = fmaxf(M, sm_m[ww][j]);
+      float num = 0.f, den = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int ww = 0; ww < NW; ++ww) {
+          const float wt = ex2(sm_m[ww][j] - M);
+          den = fmaf(wt, sm_l[ww][j], den);
+          num = fmaf(wt, sm_o[ww][j][d], num);
+        }
+      }
+      const long long row = (long long)it.b * p.Hq + (long long)it.kvh * GS + hg0 + j;
+      if (it.nparts == 1) {
+        out[row * D + d] = from_float<T>(den > 0.f ? num / den : 0.f);
+      } else {
+        const long long pr = row * p.max_parts + it.part;
+        p.part_o[pr * D + d] = num;
+        if (d == 0) {
+          p.part_ml[2 * pr] = M;
+          p.part_ml[2 * pr + 1] = den;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ════════════════════════════════════════════════════════════════════════
+// Fast path: fp16, page size 16, head size D in {64, 128, 256}.
+//
+// Warp specialisation: warp NWC is the producer; one lane streams the
+// item's pages through a STAGES-deep ring with TMA (one 16 x 64 box per 64
+// dims of K and of V, 128-byte swizzle, completion on the stage's mbarrier).
+// Warps 0..NWC-1 consume pages round-robin. Per page a consumer computes
+//   S^T (16 tokens x 8 heads) = K_page (16 x D) . Q^T (D x 8)      [mma.sync]
+// runs the online softmax on the fragments, transposes P with movmatrix and
+//   O^T (D x 8 heads) += V_page^T (D x 16) . P^T (16 x 8)           [mma.sync]
+// with P split as fp16 hi + lo so the PV product carries fp32-level accuracy.
+// Each page of a KV head is read from HBM exactly once for all GS query heads.
+// ════════════════════════════════════════════════════════════════════════
+
+// Shared-memory byte offset of the 16-byte chunk `chunk` (along d) of token
+// row `tok` in a page tile written by TMA with 128-byte swizzle: the tile is
+// D/64 boxes of 16 rows x 128 bytes, and within each 1024-byte group the
+// chunk index is XORed with the row index mod 8.
+__device__ __forceinline__ uint32_t tile_off(int tok, int chunk) {
+  return (uint32_t)((chunk >> 3) * 2048 + tok * 128 + (((chunk & 7) ^ (tok & 7)) << 4));
+}
+
+template <int D, int NT, int STAGES, int NWC>
+struct FastCfg {
+  static constexpr int kTile = 16 * D * 2;     // bytes of one K (or V) page
+  static constexpr int kStage = 2 * kTile;     // K + V
+  static constexpr int kKSteps = D / 16;
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kRing = STAGES * kStage;
+  static constexpr int kMerge = NWC * NT * 8 * (D + 4) * 4 + NWC * NT * 8 * 8;
+  static constexpr int kBarOff = kRing > kMerge ? kRing : kMerge;
+  static constexpr int kSmem = 1024 + kBarOff + STAGES * 16 + STAGES * 4;
+  static constexpr int kThreads = (NWC + 1) * 32;
+};
+
+template <int D, int NT, int STAGES, int NWC>
+__global__ void __launch_bounds__((NWC + 1) * 32)
+    pa_tma_mma_kernel(const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using C = FastCfg<D, NT, STAGES, NWC>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  int* meta = reinterpret_cast<int*>(smem + C::kBarOff + STAGES * 16);
+
+  Item it;
+  const ItemKind kind = decode_item(p, blockIdx.x, it);
+  if (kind == kItemNone) return;
+  const int GS = p.GS;
+  __half* out = static_cast<__half*>(p.out);
+  if (kind == kItemZero) {
+    __half* dst = out + ((long long)it.b * p.Hq + (long long)it.kvh * GS) * D;
+    for (int e = threadIdx.x; e < GS * D; e += blockDim.x) dst[e] = __float2half_rn(0.f);
+    return;
+  }
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar_full = smem_u32(smem + C::kBarOff);
+  const uint32_t bar_empty = bar_full + 8 * STAGES;
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int np = it.page_end - it.page_begin;
+  const uint64_t budget = p.timeout_ns;
+
+  if (warp == NWC) {
+    // ── producer ──────────────────────────────────────────────────────
+    if (lane == 0) {
+      tmap_prefetch(&tmK);
+      tmap_prefetch(&tmV);
+    }
+    const int* bt_row = p.block_tables + (long long)it.b * p.max_blocks;
+    int ent = -1;
+    int ok = 1, issued = 0;
+    for (int j = 0; j < np; ++j) {
+      if ((j & 31) == 0) {
+        const int idx = it.page_begin + j + lane;
+        ent = idx < it.page_end ? __ldg(bt_row + idx) : -1;
+      }
+      const int phys = __shfl_sync(0xffffffffu, ent, j & 31);
+      if (lane == 0) {
+        const int s = j % STAGES;
+        if (j >= STAGES && !mbar_wait(bar_empty + 8 * s, ((j / STAGES) + 1) & 1, budget)) {
+          raise_status(p, kDevTimeout);
+          ok = 0;
+        } else {
+          const bool valid = phys >= 0 && (p.num_blocks <= 0 || phys < p.num_blocks);
+          meta[s] = valid ? 1 : 0;
+          if (valid) {
+            const uint32_t full = bar_full + 8 * s;
+            mbar_arrive_expect_tx(full, C::kStage);
+            const uint32_t tk = sbase + s * C::kStage, tv = tk + C::kTile;
+#pragma unroll
+            for (int x = 0; x < C::kBoxes; ++x) {
+              tma_load_4d(tk + x * 2048, &tmK, x * 64, 0, it.kvh, phys, full);
+              tma_load_4d(tv + x * 2048, &tmV, x * 64, 0, it.kvh, phys, full);
+            }
+          } else {
+            raise_status(p, kDevBadPage);
+            mbar_arrive(bar_full + 8 * s);
+          }
+          issued = j + 1;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+    }
+    if (!ok && lane == 0) {
+      // Let copies already in flight land before the CTA can retire.
+      for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+        (void)mbar_wait(bar_full + 8 * (j % STAGES), (j / STAGES) & 1, budget);
+    }
+    return;
+  }
+
+  // ── consumers ──────────────────────────────────────────────────────
+  const int g = lane >> 2, c = lane & 3;
+  const __half* qrow =
+      static_cast<const __half*>(p.q) + ((long long)it.b * p.Hq + (long long)it.kvh * GS) * D;
+  // Q^T as the B operand (k = d, n = head): lane (g, c) holds
+  // Q[head g][16ks + 2c, +1] and Q[head g][16ks + 8 + 2c, +1].
+  uint32_t qf[NT][C::kKSteps][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int head = nt * 8 + g;
+#pragma unroll
+    for (int ks = 0; ks < C::kKSteps; ++ks) {
+      if (head < GS) {
+        const __half* qp = qrow + head * D + ks * 16 + 2 * c;
+        qf[nt][ks][0] = __ldg(reinterpret_cast<const unsigned int*>(qp));
+        qf[nt][ks][1] = __ldg(reinterpret_cast<const unsigned int*>(qp + 8));
+      } else {
+        qf[nt][ks][0] = 0u;
+        qf[nt][ks][1] = 0u;
+      }
+    }
+  }
+
+  float o[NT][C::kKSteps][4];
+  float mrun[NT][2], lrun[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int mt = 0; mt < C::kKSteps; ++mt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) o[nt][mt][r] = 0.f;
+    mrun[nt][0] = mrun[nt][1] = -INFINITY;
+    lrun[nt][0] = lrun[nt][1] = 0.f;
+  }
+
+  const float sl2 = p.scale_log2;
+  const int tok_begin = it.page_begin * 16;
+  const int mi = lane >> 3, r8 = lane & 7;
+  for (int j = warp; j < np; j += NWC) {
+    const int s = j % STAGES;
+    if (!mbar_wait(bar_full + 8 * s, (j / STAGES) & 1, budget)) {
+      raise_status(p, kDevTimeout);
+      break;
+    }
+    if (meta[s]) {
+      const uint32_t tk = sbase + s * C::kStage, tv = tk + C::kTile;
+      const int ntok = min(16, it.L - (tok_begin + j * 16));
+
+      // S^T = K . Q^T. A operand rows = tokens: matrices (tok 0-7 | 8-15) x
+      // (d lo | hi) -> a0..a3.
+      float sc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < C::kKSteps; ++ks) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(tk + tile_off(r8 + ((mi & 1) << 3), 2 * ks + (mi >> 1)), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          mma_f16_16816(sc[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
+      }
+
+      if (ntok < 16) {
+        // Last page of the sequence: slots >= ntok hold whatever the pool
+        // holds; clear them in V so 0 * (inf or NaN) cannot enter PV.
+        const int nclr = (16 - ntok) * C::kBoxes * 8;
+        for (int idx = lane; idx < nclr; idx += 32) {
+          const int row = ntok + idx / (C::kBoxes * 8);
+          const int rem = idx % (C::kBoxes * 8);
+          const uint32_t addr = tv + (rem >> 3) * 2048 + row * 128 + (rem & 7) * 16;
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
+        }
+        __syncwarp();
+      }
+
+      // Online softmax. Lane (g, c): tokens g, g+8; heads 2c, 2c+1 of tile nt.
+      const bool v0 = g < ntok, v1 = g + 8 < ntok;
+      uint32_t pb[NT][2], pl[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const float x0 = v0 ? sc[nt][0] * sl2 : -INFINITY;
+        const float x1 = v0 ? sc[nt][1] * sl2 : -INFINITY;
+        const float x2 = v1 ? sc[nt][2] * sl2 : -INFINITY;
+        const float x3 = v1 ? sc[nt][3] * sl2 : -INFINITY;
+        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
+        const float mn0 = fmaxf(mrun[nt][0], mx0), mn1 = fmaxf(mrun[nt][1], mx1);
+        const float al0 = ex2(mrun[nt][0] - mn0), al1 = ex2(mrun[nt][1] - mn1);
+        const float p0 = ex2(x0 - mn0), p1 = ex2(x1 - mn1);
+        const float p2 = ex2(x2 - mn0), p3 = ex2(x3 - mn1);
+        lrun[nt][0] = fmaf(lrun[nt][0], al0, p0 + p2);
+        lrun[nt][1] = fmaf(lrun[nt][1], al1, p1 + p3);
+        mrun[nt][0] = mn0;
+        mrun[nt][1] = mn1;
+#pragma unroll
+        for (int mt = 0; mt < C::kKSteps; ++mt) {
+          o[nt][mt][0] *= al0;
+          o[nt][mt][1] *= al1;
+          o[nt][mt][2] *= al0;
+          o[nt][mt][3] *= al1;
+        }
+        // P^T as the B operand (k = token, n = head): transpose the
+        // (token x head) accumulator pairs with movmatrix.
+        const uint32_t h01 = pack_half2(p0, p1), h23 = pack_half2(p2, p3);
+        const float2 f01 = unpack_half2(h01), f23 = unpack_half2(h23);
+        pb[nt][0] = movmatrix_trans(h01);
+        pb[nt][1] = movmatrix_trans(h23);
+        pl[nt][0] = movmatrix_trans(pack_half2(p0 - f01.x, p1 - f01.y));
+        pl[nt][1] = movmatrix_trans(pack_half2(p2 - f23.x, p3 - f23.y));
+      }
+
+      // O^T += V^T . P^T. A operand rows = d: transposed loads of matrices
+      // (tok 0-7 | 8-15) x (d lo | hi) -> a0 (d lo, tok lo), a1 (d hi, tok lo),
+      // a2 (d lo, tok hi), a3 (d hi, tok hi).
+#pragma unroll
+      for (int mt = 0; mt < C::kKSteps; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_trans(tv + tile_off(r8 + ((mi >> 1) << 3), 2 * mt + (mi & 1)), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_f16_16816(o[nt][mt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+          mma_f16_16816(o[nt][mt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+        }
+      }
+      if (ntok < 16) fence_proxy_async_smem();
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_empty + 8 * s);
+  }
+
+  // ── merge the consumer warps' states ─────────────────────────────────
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1)
+        lrun[nt][k] += __shfl_xor_sync(0xffffffffu, lrun[nt][k], off);
+
+  named_bar_sync(1, NWC * 32);  // every consumer is done with the ring
+  constexpr int RS = D + 4;     // padded row: conflict-free stores below
+  float* sm_o = reinterpret_cast<float*>(smem);  // [NWC][GS][RS]
+  float* sm_ml = sm_o + NWC * GS * RS;           // [NWC][GS][2]
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int head = nt * 8 + 2 * c + k;
+      if (head < GS) {
+        float* row = sm_o + (warp * GS + head) * RS;
+#pragma unroll
+        for (int mt = 0; mt < C::kKSteps; ++mt) {
+          row[mt * 16 + g] = o[nt][mt][k];
+          row[mt * 16 + g + 8] = o[nt][mt][2 + k];
+        }
+        if (g == 0) {
+          sm_ml[(warp * GS + head) * 2] = mrun[nt][k];
+          sm_ml[(warp * GS + head) * 2 + 1] = lrun[nt][k];
+        }
+      }
+    }
+  }
+  named_bar_sync(1, NWC * 32);
+
+  const long long row0 = (long long)it.b * p.Hq + (long long)it.kvh * GS;
+  for (int e = threadIdx.x; e < GS * D; e += NWC * 32) {
+    const int head = e / D, d = e - head * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int ww = 0; ww < NWC; ++ww) M = fmaxf(M, sm_ml[(ww * GS + head) * 2]);
+    float num = 0.f, den = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int ww = 0; ww < NWC; ++ww) {
+        const float wt = ex2(sm_ml[(ww * GS + head) * 2] - M);
+        den = fmaf(wt, sm_ml[(ww * GS + head) * 2 + 1], den);
+        num = fmaf(wt, sm_o[(ww * GS + head) * RS + d], num);
+      }
+    }
+    if (it.nparts == 1) {
+      out[(row0 + head) * D + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+    } else {
+      const long long pr = (row0 + head) * p.max_parts + it.part;
+      p.part_o[pr * D + d] = num;
+      if (d == 0) {
+        p.part_ml[2 * pr] = M;
+        p.part_ml[2 * pr + 1] = den;
+      }
+    }
+  }
+}
+
+// ════════════════════════════════════════════════════════════════════════
+// Log-sum-exp reduce of split-context partials: one CTA per (b, q head).
+//   M = max_p m_p,  w_p = 2^(m_p - M),  out = sum_p w_p o_p / sum_p w_p l_p
+// ════════════════════════════════════════════════════════════════════════
+template <typename T>
+__global__ void __launch_bounds__(128) pa_reduce_kernel(const Params p) {
+  extern __shared__ float sm_w[];  // [max_parts]
+  __shared__ float sh_M, sh_den;
+  const long long row = blockIdx.x;
+  const int b = (int)(row / p.Hq);
+  int L = __ldg(p.seq_lens + b);
+  const long long cap = (long long)p.max_blocks * p.block_size;
+  L = L < 0 ? 0 : ((long long)L > cap ? (int)cap : L);
+  const int npages = (L + p.block_size - 1) / p.block_size;
+  const int nparts = (npages + p.part_pages - 1) / p.part_pages;
+  if (nparts <= 1) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* ml = p.part_ml + row * p.max_parts * 2;
+  if (warp == 0) {
+    float M = -INFINITY;
+    for (int i = lane; i < nparts; i += 32) M = fmaxf(M, ml[2 * i]);
+    M = warp_max(M);
+    if (lane == 0) sh_M = M;
+  }
+  __syncthreads();
+  const float M = sh_M;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+    const float mp = ml[2 * i];
+    sm_w[i] = (M == -INFINITY || mp == -INFINITY) ? 0.f : ex2(mp - M);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float den = 0.f;
+    for (int i = lane; i < nparts; i += 32) den = fmaf(sm_w[i], ml[2 * i + 1], den);
+    den = warp_sum(den);
+    if (lane == 0) sh_den = den;
+  }
+  __syncthreads();
+  const float den = sh_den;
+  const float* po = p.part_o + row * p.max_parts * p.D;
+  T* out = static_cast<T*>(p.out) + row * p.D;
+  for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int i = 0; i < nparts; ++i) acc = fmaf(sm_w[i], po[(long long)i * p.D + d], acc);
+    out[d] = from_float<T>(den > 0.f ? acc / den : 0.f);
+  }
+}
+
+// ════════════════════════════════════════════════════════════════════════
+// Launchers
+// ════════════════════════════════════════════════════════════════════════
+namespace {
+
+template <typename T, int DPL, int HG>
+cudaError_t launch_generic_t(const Params& p, cudaStream_t st) {
+  const long long grid = (long long)p.B * p.Hkv * p.max_parts;
+  pa_generic_kernel<T, DPL, HG><<<(unsigned)grid, 128, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T, int DPL>
+cudaError_t launch_generic_dpl(const Params& p, cudaStream_t st) {
+  // Heads per pass: enough to cover the group, with HG*DPL <= 32 registers
+  // of accumulator per lane.
+  constexpr int HGMAX = 32 / DPL;
+  int hg = 1;
+  while (hg < p.GS && hg < HGMAX) hg <<= 1;
+  switch (hg) {
+    case 1: return launch_generic_t<T, DPL, 1>(p, st);
+    case 2: return launch_generic_t<T, DPL, 2>(p, st);
+    case 4: return launch_generic_t<T, DPL, 4>(p, st);
+    case 8: return launch_generic_t<T, DPL, (HGMAX >= 8 ? 8 : HGMAX)>(p, st);
+    default: return launch_generic_t<T, DPL, (HGMAX >= 16 ? 16 : HGMAX)>(p, st);
+  }
+}
+
+template <typename T>
+cudaError_t launch_generic_typed(const Params& p, cudaStream_t st) {
+  if (p.D <= 32) return launch_generic_dpl<T, 1>(p, st);
+  if (p.D <= 64) return launch_generic_dpl<T, 2>(p, st);
+  if (p.D <= 128) return launch_generic_dpl<T, 4>(p, st);
+  return launch_generic_dpl<T, 8>(p, st);
+}
+
+template <int D, int NT>
+cudaError_t launch_fast_t(const CUtensorMap& tk, const CUtensorMap& tv, const Params& p,
+                          cudaStream_t st) {
+  constexpr int STAGES = (D == 256) ? 4 : 8;
+  constexpr int NWC = 4;
+  using C = FastCfg<D, NT, STAGES, NWC>;
+  auto kern = pa_tma_mma_kernel<D, NT, STAGES, NWC>;
+  // The attribute is per function and device; setting it every call costs
+  // a driver call only.
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return e;
+  const long long grid = (long long)p.B * p.Hkv * p.max_parts;
+  kern<<<(unsigned)grid, C::kThreads, C::kSmem, st>>>(tk, tv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_generic(const Params& p, int dtype_size, cudaStream_t st) {
+  return dtype_size == 4 ? launch_generic_typed<float>(p, st)
+                         : launch_generic_typed<__half>(p, st);
+}
+
+bool fast_path_shape_ok(int head_size, int group, int block_size, int dtype_size) {
+  if (dtype_size != 2 || block_size != 16) return false;
+  if (head_size != 64 && head_size != 128 && head_size != 256) return false;
+  if (group < 1 || group > 16) return false;
+  if (group > 8 && head_size == 256) return false;  // accumulator registers
+  return true;
+}
+
+cudaError_t launch_fast(const CUtensorMap& tk, const CUtensorMap& tv, const Params& p,
+                        cudaStream_t st) {
+  const bool two = p.GS > 8;
+  switch (p.D) {
+    case 64: return two ? launch_fast_t<64, 2>(tk, tv, p, st) : launch_fast_t<64, 1>(tk, tv, p, st);
+    case 128: return two ? launch_fast_t<128, 2>(tk, tv, p, st) : launch_fast_t<128, 1>(tk, tv, p, st);
+    case 256: return launch_fast_t<256, 1>(tk, tv, p, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_reduce(const Params& p, int dtype_size, cudaStream_t st) {
+  const long long grid = (long long)p.B * p.Hq;
+  const size_t smem = (size_t)p.max_parts * sizeof(float);
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  if (dtype_size == 4)
+    pa_reduce_kernel<float><<<(unsigned)grid, 128, smem, st>>>(p);
+  else
+    pa_reduce_kernel<__half><<<(unsigned)grid, 128, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace xpa

@@ -1,0 +1,255 @@
+"""Host-side mirror of the xLLMs paged-attention operator interface.
+
+Three layers, all calling the C ABI of libxpa.so (include/operator_api.h):
+
+* :func:`nxt_paged_attention`, :func:`nxt_paged_attention_v2`,
+  :func:`nxt_paged_attention_flash` — the reference's entry points
+  (include/operator_api.h:63-115 of the xLLMs project) with the same
+  argument names, order and meaning. Pointer arguments accept torch CUDA
+  tensors or raw device addresses. Unlike the reference (which returns
+  nothing and checks nothing), a rejected call raises :class:`PagedAttentionError`.
+* :func:`paged_attention` — tensor-level convenience over the status-returning
+  ``nxt_paged_attention_ex`` that derives sizes and strides from the tensors.
+* :class:`CudaBackendPlugin` — the dlopen'd plugin path
+  (backends/cuda_backend.c:35-120), driven the way the reference's backend
+  manager drives it (src/core/backend_manager.c:264-344).
+
+torch is used for device memory and streams only; all arithmetic happens in
+the native kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Union
+
+from . import _native
+
+Pointer = Union[int, None, "torch.Tensor"]  # noqa: F821
+
+
+class PagedAttentionError(RuntimeError):
+    def __init__(self, code: int, where: str):
+        self.code = code
+        super().__init__(f"{where}: {_native.strerror(code)} ({code})")
+
+
+def _ptr(x: Pointer) -> Optional[int]:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+def _stream_ptr(stream) -> Optional[int]:
+    if stream is None:
+        try:
+            import torch
+            if torch.cuda.is_available() and torch.cuda.is_initialized():
+                return torch.cuda.current_stream().cuda_stream
+        except ImportError:  # pragma: no cover
+            pass
+        return None
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def _dropin(name: str, out, query, key_cache, value_cache, block_tables, seq_lens,
+            num_seqs, num_heads, head_size, num_kv_heads, scale, max_num_blocks_per_seq,
+            block_size, dtype_size, kv_block_stride, kv_head_stride, stream=None) -> None:
+    lib = _native.xpa()
+    getattr(lib, name)(
+        _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+        _ptr(seq_lens), int(num_seqs), int(num_heads), int(head_size), int(num_kv_heads),
+        float(scale), int(max_num_blocks_per_seq), int(block_size), int(dtype_size),
+        int(kv_block_stride), int(kv_head_stride), _stream_ptr(stream))
+    rc = lib.nxt_paged_attention_last_error()
+    if rc != _native.NXT_PA_OK:
+        raise PagedAttentionError(rc, name)
+
+
+def nxt_paged_attention(out, query, key_cache, value_cache, block_tables, seq_lens,
+                        num_seqs, num_heads, head_size, num_kv_heads, scale,
+                        max_num_blocks_per_seq, block_size, dtype_size, kv_block_stride,
+                        kv_head_stride, stream=None) -> None:
+    """Reference ``nxt_paged_attention`` (operators/page_attention.cu:170)."""
+    _dropin("nxt_paged_attention", out, query, key_cache, value_cache, block_tables, seq_lens,
+            num_seqs, num_heads, head_size, num_kv_heads, scale, max_num_blocks_per_seq,
+            block_size, dtype_size, kv_block_stride, kv_head_stride, stream)
+
+
+def nxt_paged_attention_v2(out, query, key_cache, value_cache, block_tables, seq_lens,
+                           num_seqs, num_heads, head_size, num_kv_heads, scale,
+                           max_num_blocks_per_seq, block_size, dtype_size, kv_block_stride,
+                           kv_head_stride, stream=None) -> None:
+    """Reference ``nxt_paged_attention_v2`` (operators/page_attention_v2.cu:262)."""
+    _dropin("nxt_paged_attention_v2", out, query, key_cache, value_cache, block_tables,
+            seq_lens, num_seqs, num_heads, head_size, num_kv_heads, scale,
+            max_num_blocks_per_seq, block_size, dtype_size, kv_block_stride, kv_head_stride,
+            stream)
+
+
+def nxt_paged_attention_flash(out, query, key_cache, value_cache, block_tables, seq_lens,
+                              num_seqs, num_heads, head_size, num_kv_heads, scale,
+                              max_num_blocks_per_seq, block_size, dtype_size, kv_block_stride,
+                              kv_head_stride, stream=None) -> None:
+    """Reference ``nxt_paged_attention_flash`` (operators/flashinfer_adapter.cu:329)."""
+    _dropin("nxt_paged_attention_flash", out, query, key_cache, value_cache, block_tables,
+            seq_lens, num_seqs, num_heads, head_size, num_kv_heads, scale,
+            max_num_blocks_per_seq, block_size, dtype_size, kv_block_stride, kv_head_stride,
+            stream)
+
+
+def _dtype_size(t) -> int:
+    import torch
+    if t.dtype == torch.float16:
+        return 2
+    if t.dtype == torch.float32:
+        return 4
+    raise PagedAttentionError(_native.NXT_PA_EINVAL, f"dtype {t.dtype}")
+
+
+def paged_attention(query, key_cache, value_cache, block_tables, seq_lens, *,
+                    scale: Optional[float] = None, out=None, num_blocks: Optional[int] = None,
+                    workspace=None, device_status=None, stream=None):
+    """Decode attention of one new token per sequence over a paged KV cache.
+
+    query [B, Hq, D]; key_cache/value_cache [num_blocks, Hkv, block_size, D]
+    (contiguous, the reference layout); block_tables [B, max_blocks] int32;
+    seq_lens [B] int32; all on the same CUDA device. Returns out [B, Hq, D] in
+    query's dtype. ``scale`` defaults to 1/sqrt(D). ``num_blocks`` defaults to
+    key_cache.shape[0], which lets the kernels mask out-of-range pages.
+    """
+    import torch
+    B, Hq, D = query.shape
+    nb, Hkv, bs, Dk = key_cache.shape
+    if Dk != D or tuple(value_cache.shape) != tuple(key_cache.shape):
+        raise PagedAttentionError(_native.NXT_PA_EINVAL, "paged_attention: cache shapes")
+    if not (key_cache.is_contiguous() and value_cache.is_contiguous() and query.is_contiguous()):
+        raise PagedAttentionError(_native.NXT_PA_EINVAL, "paged_attention: non-contiguous input")
+    if out is None:
+        out = torch.empty_like(query)
+    ds = _dtype_size(query)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    ws_bytes = 0
+    if workspace is not None:
+        ws_bytes = workspace.numel() * workspace.element_size()
+    rc = _native.xpa().nxt_paged_attention_ex(
+        _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+        _ptr(seq_lens), B, Hq, D, Hkv, float(scale), block_tables.shape[1], bs, ds,
+        Hkv * bs * D, bs * D, nb if num_blocks is None else int(num_blocks),
+        _ptr(workspace), ws_bytes, _ptr(device_status), _stream_ptr(stream))
+    if rc != _native.NXT_PA_OK:
+        raise PagedAttentionError(rc, "nxt_paged_attention_ex")
+    return out
+
+
+def workspace_size(num_seqs, num_heads, head_size, num_kv_heads, max_num_blocks_per_seq,
+                   block_size=16, dtype_size=2) -> int:
+    return int(_native.xpa().nxt_paged_attention_workspace_size(
+        num_seqs, num_heads, head_size, num_kv_heads, max_num_blocks_per_seq, block_size,
+        dtype_size))
+
+
+def kernel_path(key_cache, value_cache, num_heads, head_size, num_kv_heads, block_size,
+                dtype_size, kv_block_stride, kv_head_stride) -> int:
+    """NXT_PA_PATH_* the kernels take for these arguments."""
+    return int(_native.xpa().nxt_paged_attention_path(
+        _ptr(key_cache), _ptr(value_cache), num_heads, head_size, num_kv_heads, block_size,
+        dtype_size, kv_block_stride, kv_head_stride))
+
+
+def device_status(clear: bool = True) -> int:
+    """NXT_PA_DEV_* bits of the current device's library status word."""
+    rc = _native.xpa().nxt_paged_attention_device_status(1 if clear else 0)
+    if rc < 0:
+        raise PagedAttentionError(rc, "nxt_paged_attention_device_status")
+    return rc
+
+
+# ── plugin path ───────────────────────────────────────────────────────────
+class NxtBackend(ctypes.Structure):
+    """Layout of the reference's NxtBackend (include/backend.h:141-151)."""
+    _fields_ = [
+        ("name", ctypes.c_char_p),
+        ("so_path", ctypes.c_char_p),
+        ("dl_handle", ctypes.c_void_p),
+        ("api", ctypes.c_void_p * 8),
+        ("state", ctypes.c_int),
+        ("priority", ctypes.c_int32),
+        ("model_count", ctypes.c_uint32),
+        ("models", ctypes.c_void_p),
+        ("backend_state", ctypes.c_void_p),
+    ]
+
+
+class NxtPagedAttentionInput(ctypes.Structure):
+    """Layout of the reference's NxtPagedAttentionInput (backends/cuda_backend.h:29-46)."""
+    _fields_ = [
+        ("query", ctypes.c_void_p),
+        ("key_cache", ctypes.c_void_p),
+        ("value_cache", ctypes.c_void_p),
+        ("block_tables", ctypes.c_void_p),
+        ("seq_lens", ctypes.c_void_p),
+        ("num_seqs", ctypes.c_int),
+        ("num_heads", ctypes.c_int),
+        ("head_size", ctypes.c_int),
+        ("num_kv_heads", ctypes.c_int),
+        ("scale", ctypes.c_float),
+        ("max_num_blocks_per_seq", ctypes.c_int),
+        ("block_size", ctypes.c_int),
+        ("dtype_size", ctypes.c_int),
+        ("kv_block_stride", ctypes.c_int),
+        ("kv_head_stride", ctypes.c_int),
+        ("stream", ctypes.c_void_p),
+    ]
+
+
+NXT_BACKEND_STATE_UNINITIALIZED = 0
+NXT_BACKEND_STATE_READY = 2
+
+
+class CudaBackendPlugin:
+    """libxllm_cuda_backend.so driven like the reference backend manager does:
+    init on load, run(input descriptor, output), fini on unload."""
+
+    def __init__(self, name: str = "cuda"):
+        self.lib = _native.plugin()
+        self.backend = NxtBackend()
+        self.backend.name = name.encode()
+        self.backend.so_path = _native.PLUGIN_PATH.encode()
+        rc = self.lib.nxt_backend_init(ctypes.byref(self.backend))
+        if rc != 0:
+            raise PagedAttentionError(_native.NXT_PA_ECUDA, "nxt_backend_init")
+
+    def run(self, pa: NxtPagedAttentionInput, output: Pointer) -> int:
+        return int(self.lib.nxt_backend_run(ctypes.byref(self.backend), ctypes.byref(pa),
+                                            _ptr(output)))
+
+    def close(self) -> int:
+        return int(self.lib.nxt_backend_fini(ctypes.byref(self.backend)))
+
+
+def make_input(query, key_cache, value_cache, block_tables, seq_lens, scale=None,
+               stream=None) -> NxtPagedAttentionInput:
+    """Fills the plugin's input descriptor from tensors in the reference layout."""
+    B, Hq, D = query.shape
+    nb, Hkv, bs, _ = key_cache.shape
+    pa = NxtPagedAttentionInput()
+    pa.query = _ptr(query)
+    pa.key_cache = _ptr(key_cache)
+    pa.value_cache = _ptr(value_cache)
+    pa.block_tables = _ptr(block_tables)
+    pa.seq_lens = _ptr(seq_lens)
+    pa.num_seqs, pa.num_heads, pa.head_size, pa.num_kv_heads = B, Hq, D, Hkv
+    pa.scale = 1.0 / math.sqrt(D) if scale is None else scale
+    pa.max_num_blocks_per_seq = block_tables.shape[1]
+    pa.block_size = bs
+    pa.dtype_size = _dtype_size(query)
+    pa.kv_block_stride = Hkv * bs * D
+    pa.kv_head_stride = bs * D
+    pa.stream = _stream_ptr(stream)
+    return pa
