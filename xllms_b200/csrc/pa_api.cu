@@ -12,6 +12,7 @@
 #include <utility>
 
 #include "operator_api.h"
+#include "pa_host.h"
 #include "pa_launch.h"
 
 namespace {
@@ -41,7 +42,17 @@ std::map<std::pair<int, uintptr_t>, Workspace> g_ws;
 
 int map_cuda(cudaError_t e) { return e == cudaSuccess ? NXT_PA_OK : NXT_PA_ECUDA; }
 
+}  // namespace
+
+namespace xpa {
+namespace host {
+
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
+
+}  // namespace host
+}  // namespace xpa
+
+namespace {
 
 // Per-device facts; status word allocated on first use. Caller holds g_mu.
 int device_state_locked(int dev, DeviceState** out) {
@@ -67,6 +78,11 @@ int device_state_locked(int dev, DeviceState** out) {
   return NXT_PA_OK;
 }
 
+}  // namespace
+
+namespace xpa {
+namespace host {
+
 int sm_count_of(int dev) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (dev < 0 || dev >= kMaxDevices) return 148;
@@ -80,12 +96,6 @@ int sm_count_of(int dev) {
   }
   return d.sm_count;
 }
-
-struct Plan {
-  int part_pages = 32;
-  int max_parts = 1;
-  size_t ws_bytes = 0;
-};
 
 // Partition size: 32 pages (512 tokens at page size 16) by default, halved
 // while the grid would leave the GPU short of work, and doubled while the
@@ -161,6 +171,13 @@ int check_args(const void* out, const void* q, const void* k, const void* v, con
   if (kbs < 0 || khs < 0) return NXT_PA_EINVAL;
   return NXT_PA_OK;
 }
+
+}  // namespace host
+}  // namespace xpa
+
+using namespace xpa::host;
+
+namespace {
 
 int run(void* out, const void* q, const void* k, const void* v, const int* bt, const int* sl,
         int B, int Hq, int D, int Hkv, float scale, int max_blocks, int bs, int ds,

@@ -1,0 +1,37 @@
+// pa_host.h — host-side planning helpers shared by the C-ABI entry points
+// (pa_api.cu) and the allocation-free entry point (pa_noalloc.cu).
+#pragma once
+
+#include <cuda.h>
+#include <stddef.h>
+
+namespace xpa {
+namespace host {
+
+int ceil_div(long long a, long long b);
+
+// SM count of device `dev` (cached; 148 when the query fails).
+int sm_count_of(int dev);
+
+// Context partitioning of one call and the split-context partial bytes it needs.
+struct Plan {
+  int part_pages = 32;
+  int max_parts = 1;
+  size_t ws_bytes = 0;
+};
+Plan make_plan(int B, int Hq, int D, int Hkv, int max_blocks, int nsm);
+
+// Tensor map of one fp16 pool for the TMA path; false when it cannot be encoded.
+bool encode_pool(CUtensorMap* m, const void* base, int D, int Hkv, long long num_blocks,
+                 long long kbs, long long khs);
+
+// Pool alignment and stride order the TMA path needs.
+bool fast_layout_ok(const void* k, const void* v, int D, int Hkv, long long kbs, long long khs);
+
+// NXT_PA_OK or NXT_PA_EINVAL for the argument set of one call.
+int check_args(const void* out, const void* q, const void* k, const void* v, const int* bt,
+               const int* sl, int B, int Hq, int D, int Hkv, int max_blocks, int bs, int ds,
+               long long kbs, long long khs);
+
+}  // namespace host
+}  // namespace xpa
