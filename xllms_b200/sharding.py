@@ -24,6 +24,15 @@ def head_range(num_heads: int, world_size: int, rank: int) -> Tuple[int, int]:
     return rank * n, (rank + 1) * n
 
 
+def shard_heads(q, k, v, num_kv_heads: int, world_size: int, rank: int):
+    """Rank `rank`'s slice of full inputs: q [B, Hq, D] -> its query heads,
+    pools [NB, Hkv, P, D] -> its KV heads (same page ids). Returns copies."""
+    Hq = q.shape[1]
+    q0, q1 = head_range(Hq, world_size, rank)
+    k0, k1 = head_range(num_kv_heads, world_size, rank)
+    return q[:, q0:q1].copy(), k[:, k0:k1].copy(), v[:, k0:k1].copy()
+
+
 def gather_heads(out_local, gathered=None, group=None):
     """All-gathers every rank's [B, Hq/P, D] slice; returns [P, B, Hq/P, D]."""
     import torch
@@ -32,7 +41,10 @@ def gather_heads(out_local, gathered=None, group=None):
     if gathered is None:
         gathered = torch.empty((P,) + tuple(out_local.shape), dtype=out_local.dtype,
                                device=out_local.device)
-    dist.all_gather_into_tensor(gathered, out_local.contiguous(), group=group)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(gathered, out_local.contiguous(), group=group)
+    else:
+        dist.all_gather(list(gathered.unbind(0)), out_local.contiguous(), group=group)
     return gathered
 
 
