@@ -49,6 +49,10 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=6.0,
                     help="wall-time budget of the cpu_baseline leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the e2e leg (profiling runs)")
+    ap.add_argument("--seqs", type=int, default=0,
+                    help="sequences per GPU for c2/c4/c5 (default: the BASELINE size); smaller "
+                         "values make the small cases the ncu captures run on")
     return ap.parse_args()
 
 
@@ -61,14 +65,16 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def make_batch(workload: str, world: int, rank: int):
+def make_batch(workload: str, world: int, rank: int, seqs: int = 0):
     from xllms_b200 import workloads as W
     if workload == "c2":
-        return W.config2(num_seqs=64 * world, world_size=world, rank=rank)
+        return W.config2(num_seqs=(seqs or 64) * world, world_size=world, rank=rank)
     if workload == "c5":
-        return W.config5(world_size=world, rank=rank)
+        return W.config5(world_size=world, rank=rank, num_seqs=seqs or 512)
     if world > 1:
         raise SystemExit(f"workload {workload} runs on one GPU")
+    if workload == "c4" and seqs:
+        return W.config4(num_seqs=seqs)
     return W.CONFIGS[workload]()
 
 
@@ -227,7 +233,7 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    batch = make_batch(args.workload, world, rank)
+    batch = make_batch(args.workload, world, rank, args.seqs)
     q, k, v = batch.values_torch(dev)
     bt, sl = batch.tables_torch(dev)
     out = torch.empty_like(q)
@@ -281,11 +287,15 @@ def run_ours(args, rank, world, local_rank):
     clocks.stop()
     t_step = start.elapsed_time(stop) / K
     t_kern = statistics.mean(a.elapsed_time(b) for a, b in zip(ev_a, ev_b))
+    resident = (full if world > 1 else out).clone()  # output of the device-resident run
     st = PA.device_status(clear=True)
     if st:
         raise SystemExit(f"device status after timing: {st:#x}")
 
     # ── e2e through the backend plugin (C ABI) with host buffers ───────────
+    if args.no_e2e:
+        return _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, None,
+                       clocks, None, q, k, v, 0, 0, dev)
     plugin = PA.CudaBackendPlugin()
     q_h = q.cpu().pin_memory()
     bt_h = bt.cpu().pin_memory()
@@ -321,19 +331,28 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     clocks_e2e.stop()
     t_e2e = e_start.elapsed_time(e_stop) / K
-    if not torch.equal(out_h.to(dev), res):
+    if not torch.equal(out_h.to(dev), resident):
         raise SystemExit("e2e output differs from the device-resident run")
     plugin.close()
+    h2d = (q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + sl_h.numel() * 4)
+    d2h = out_h.numel() * out_h.element_size()
+    return _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t_e2e,
+                   clocks, clocks_e2e, q, k, v, h2d, d2h, dev)
 
+
+def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t_e2e, clocks,
+            clocks_e2e, q, k, v, h2d, d2h, dev):
+    import torch
+    import torch.distributed as dist
+    K = args.steps
     bytes_rank = batch.algorithmic_bytes()
     ub_rank = batch.algorithmic_bytes(unique=True) if args.workload == "c4" else bytes_rank
     kv_rank = batch.kv_bytes()
-    h2d = (q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + sl_h.numel() * 4)
-    d2h = out_h.numel() * out_h.element_size()
     if world > 1:
-        t = torch.tensor([t_step, t_kern, t_e2e], dtype=torch.float64, device=dev)
+        t = torch.tensor([t_step, t_kern, t_e2e or 0.0], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         t_step, t_kern, t_e2e = (float(x) for x in t.tolist())
+        t_e2e = t_e2e or None
         s = torch.tensor([bytes_rank, ub_rank, kv_rank, h2d, d2h], dtype=torch.float64,
                          device=dev)
         dist.all_reduce(s, op=dist.ReduceOp.SUM)
@@ -399,7 +418,7 @@ def run_ours(args, rank, world, local_rank):
             "traffic": None,
             "bytes_per_launch": ub_rank,
         },
-        "e2e": {
+        "e2e": None if t_e2e is None else {
             "value": round(tot_bytes / (t_e2e * 1e-3) / 1e9, 2),
             "unit": "GB/s",
             "ms_per_step": round(t_e2e, 5),
@@ -424,7 +443,7 @@ def run_reference(args, rank, world):
     arm's workload (the first 8 sequences); rank 0 only, one sample pass per step."""
     if rank != 0:
         return None
-    batch = make_batch(args.workload, world, 0)
+    batch = make_batch(args.workload, world, 0, args.seqs)
     seqs = min(8, batch.num_seqs)
     arrays = sample_arrays(batch, seqs)
     gbs, per, info = cpu_leg(batch, arrays, passes=max(1, args.steps), warmup=args.warmup)
