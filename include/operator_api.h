@@ -161,6 +161,39 @@ int nxt_paged_attention_device_status(int clear);
  * device. Synchronises each device that has one. */
 int nxt_paged_attention_release_workspaces(void);
 
+/* extension, no counterpart in the reference — paged decode attention that
+ * allocates no device memory, for callers that cannot allocate: a serving
+ * engine that has reserved nearly all of HBM for its KV page pool, or a host
+ * that routes every device allocation through its own pool, has no room for
+ * (or forbids) a library's cudaMalloc, and cudaMalloc/cudaFree synchronise
+ * the device mid decode loop. Same arguments and results as
+ * nxt_paged_attention_ex without the workspace: split-context partials live
+ * in one fixed array of NXT_PA_NOALLOC_SCRATCH_BYTES compiled into the
+ * library, which every GPU that loads it holds until the process exits.
+ *   - Limit: a call needing more partial storage than the array
+ *     (nxt_paged_attention_workspace_size(...) > NXT_PA_NOALLOC_SCRATCH_BYTES)
+ *     returns NXT_PA_ESCRATCH and launches nothing.
+ *   - The first call on each device looks up the array's device address
+ *     (set-up); make that first call before any stream capture.
+ *   - Every call shares the one array and leaves its partials there; calls
+ *     whose kernels overlap on the GPU (other streams, other host threads on
+ *     the same device) race on it. Nothing in it needs clearing between calls.
+ *   - device_status: a caller-owned device int for NXT_PA_DEV_* bits, or NULL. */
+#define NXT_PA_NOALLOC_SCRATCH_BYTES (32u << 20)
+#define NXT_PA_ESCRATCH      (-27) /* request exceeds the fixed no-alloc scratch */
+int nxt_paged_attention_noalloc(
+    void *out, const void *query,
+    const void *key_cache, const void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq,
+    int block_size, int dtype_size,
+    int64_t kv_block_stride, int64_t kv_head_stride,
+    int64_t num_blocks,
+    int *device_status,
+    nxt_stream_t stream);
+
 /* extension — instrumentation for timing the attention kernel alone. The next
  * call made by this host thread records `before` on its stream immediately
  * before the main attention kernel and `after` immediately after it (ahead of

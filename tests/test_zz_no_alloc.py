@@ -1,0 +1,93 @@
+"""nxt_paged_attention_noalloc: decode attention for callers that cannot
+allocate device memory.
+
+A serving engine that has reserved nearly all of HBM for its KV page pool, or
+a host that routes every device allocation through its own pool, cannot let a
+library call cudaMalloc (and cudaMalloc/cudaFree would synchronise the device
+in the middle of the decode loop). This entry point keeps its split-context
+partials in a fixed array compiled into the library. It is checked here
+through the C ABI against the regular entry point, on two calls in a row.
+This file is collected last on purpose.
+"""
+import numpy as np
+import pytest
+
+from _helpers import check_close, to_device
+from xllms_b200 import _native
+from xllms_b200 import operator_api as PA
+from xllms_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+
+def _noalloc(b, qt, kt, vt, bt, sl, out, status=None, max_blocks=None):
+    import torch
+    return _native.xpa().nxt_paged_attention_noalloc(
+        out.data_ptr(), qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), bt.data_ptr(),
+        sl.data_ptr(), b.num_seqs, b.num_heads, b.head_size, b.num_kv_heads, b.scale,
+        b.max_blocks if max_blocks is None else max_blocks, b.block_size, b.dtype_size,
+        b.kv_block_stride, b.kv_head_stride, b.num_blocks,
+        None if status is None else status.data_ptr(),
+        torch.cuda.current_stream().cuda_stream)
+
+
+CASES = {
+    # fp16 GQA, TMA + tensor-core kernel, sequences split into many partitions
+    "fast_fp16": lambda: W.make_batch("na16", [3000, 700, 1, 5000], 32, 8, 128, "f16", 91,
+                                      value_std=0.5),
+    # fp32 MHA, CUDA-core kernel, split as well
+    "generic_fp32": lambda: W.make_batch("na32", [2000, 33], 12, 12, 64, "f32", 92),
+}
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_noalloc_matches_regular_entry_point_on_two_calls(cuda, case):
+    import torch
+    b = CASES[case]()
+    need = PA.workspace_size(b.num_seqs, b.num_heads, b.head_size, b.num_kv_heads,
+                             b.max_blocks, b.block_size, b.dtype_size)
+    assert 0 < need <= _native.NXT_PA_NOALLOC_SCRATCH_BYTES  # the case uses the scratch
+    q, k, v = b.values_numpy()
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    regular = PA.paged_attention(qt, kt, vt, bt, sl, num_blocks=b.num_blocks)
+    torch.cuda.synchronize()
+    expect = regular.float().cpu().numpy()
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for call in range(2):
+        out = torch.full_like(qt, float("nan"))
+        assert _noalloc(b, qt, kt, vt, bt, sl, out, status) == _native.NXT_PA_OK
+        torch.cuda.synchronize()
+        check_close(out, expect, what=f"{case} call {call + 1}")
+    assert int(status.item()) == 0
+
+
+def test_noalloc_calls_allocate_nothing(cuda):
+    import torch
+    b = CASES["fast_fp16"]()
+    q, k, v = b.values_numpy()
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    outs = [torch.empty_like(qt) for _ in range(3)]
+    assert _noalloc(b, qt, kt, vt, bt, sl, outs[0]) == 0  # first call on the device: set-up
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for out in outs[1:]:
+        assert _noalloc(b, qt, kt, vt, bt, sl, out) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    assert torch.equal(outs[1], outs[2])
+
+
+def test_noalloc_rejects_requests_beyond_its_scratch(cuda):
+    import torch
+    # Llama-3-70B long-context shape: 8 x 64 heads x 8192-page rows needs ~68 MB of partials.
+    b = W.make_batch("big", [16] * 8, 64, 8, 128, "f16", 93, max_blocks=8192)
+    need = PA.workspace_size(8, 64, 128, 8, 8192, 16, 2)
+    assert need > _native.NXT_PA_NOALLOC_SCRATCH_BYTES
+    q, k, v = b.values_numpy()
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = torch.full_like(qt, 7.0)
+    rc = _noalloc(b, qt, kt, vt, bt, sl, out)
+    torch.cuda.synchronize()
+    assert rc == _native.NXT_PA_ESCRATCH
+    assert "scratch" in _native.strerror(rc)
+    assert bool((out == 7.0).all())  # nothing was launched

@@ -21,6 +21,8 @@ NXT_PA_EINVAL = -22
 NXT_PA_ENOMEM = -12
 NXT_PA_EWORKSPACE = -28
 NXT_PA_ECUDA = -5
+NXT_PA_ESCRATCH = -27
+NXT_PA_NOALLOC_SCRATCH_BYTES = 32 << 20
 NXT_PA_DEV_TIMEOUT = 0x1
 NXT_PA_DEV_BAD_PAGE = 0x2
 NXT_PA_DEV_SEQ_CLAMPED = 0x4
@@ -47,6 +49,11 @@ SIGNATURES = {
     "nxt_paged_attention_path": (_I, [_CVP, _CVP, _I, _I, _I, _I, _I, _I64, _I64]),
     "nxt_paged_attention_device_status": (_I, [_I]),
     "nxt_paged_attention_release_workspaces": (_I, []),
+    "nxt_paged_attention_noalloc": (
+        _I,
+        [_VP, _CVP, _CVP, _CVP, _IP, _IP, _I, _I, _I, _I, _F, _I, _I, _I, _I64, _I64, _I64,
+         _VP, _VP],
+    ),
     "nxt_paged_attention_profile_next": (_I, [_VP, _VP]),
     "nxt_paged_attention_device_info": (
         _I, [ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.c_char_p, _I]),

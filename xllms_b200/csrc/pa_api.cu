@@ -316,6 +316,7 @@ const char* nxt_paged_attention_strerror(int code) {
     case NXT_PA_ENOMEM: return "workspace allocation failed";
     case NXT_PA_EWORKSPACE: return "workspace smaller than required";
     case NXT_PA_ECUDA: return "CUDA call failed";
+    case NXT_PA_ESCRATCH: return "request needs more split-context scratch than the no-alloc array holds";
     default: return "unknown status";
   }
 }
