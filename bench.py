@@ -65,6 +65,20 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def ncu_traffic(workload_name: str, alg_bytes: int):
+    """DRAM read + write bytes per launch of the attention kernel from the ncu
+    capture recorded in profiles/traffic.json, when it was taken on this exact
+    workload (same algorithmic bytes); else None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            rec = json.load(f).get(workload_name)
+    except Exception:
+        return None
+    if not rec or int(rec["algorithmic_bytes_per_launch"]) != int(alg_bytes):
+        return None
+    return int(rec["dram_read_bytes_per_launch"]) + int(rec["dram_write_bytes_per_launch"])
+
+
 def make_batch(workload: str, world: int, rank: int, seqs: int = 0):
     from xllms_b200 import workloads as W
     if workload == "c2":
@@ -415,7 +429,8 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
             "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
                            else "fallback 6.65 TB/s",
             "kernel_ms": round(t_kern, 5),
-            "traffic": None,
+            "traffic": ncu_traffic(batch.name, ub_rank),
+            "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
             "bytes_per_launch": ub_rank,
         },
         "e2e": None if t_e2e is None else {

@@ -79,9 +79,9 @@ def test_noalloc_calls_allocate_nothing(cuda):
 
 def test_noalloc_rejects_requests_beyond_its_scratch(cuda):
     import torch
-    # Llama-3-70B long-context shape: 8 x 64 heads x 8192-page rows needs ~68 MB of partials.
-    b = W.make_batch("big", [16] * 8, 64, 8, 128, "f16", 93, max_blocks=8192)
-    need = PA.workspace_size(8, 64, 128, 8, 8192, 16, 2)
+    # Llama-3-70B long-context shape with 64 sequences of 8192-page rows: ~136 MB of partials.
+    b = W.make_batch("big", [16] * 64, 64, 8, 128, "f16", 93, max_blocks=8192)
+    need = PA.workspace_size(64, 64, 128, 8, 8192, 16, 2)
     assert need > _native.NXT_PA_NOALLOC_SCRATCH_BYTES
     q, k, v = b.values_numpy()
     qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)

@@ -97,13 +97,20 @@ int sm_count_of(int dev) {
   return d.sm_count;
 }
 
-// Partition size: 32 pages (512 tokens at page size 16) by default, halved
-// while the grid would leave the GPU short of work, and doubled while the
-// reduce kernel's per-row weight table would not fit its shared memory.
+// Partition size: XPA_PART_PAGES by default, halved (down to 4 pages) while
+// the grid would hold fewer than 12 items per SM (about two waves of the
+// TMA kernel's 6 resident CTAs per SM), and doubled while the reduce kernel's
+// per-row weight table would not fit its shared memory.
+// Default partition length in pages (128 pages = 2048 tokens at page size 16);
+// a build may override it with -DXPA_PART_PAGES=n for tuning sweeps.
+#ifndef XPA_PART_PAGES
+#define XPA_PART_PAGES 128
+#endif
+
 Plan make_plan(int B, int Hq, int D, int Hkv, int max_blocks, int nsm) {
   Plan pl;
   const long long mb = max_blocks > 0 ? max_blocks : 1;
-  int pp = 32;
+  int pp = XPA_PART_PAGES;
   while (pp > 4 && (long long)B * Hkv * ceil_div(mb, pp) < 12LL * nsm) pp >>= 1;
   while (ceil_div(mb, pp) > 8192) pp <<= 1;
   pl.part_pages = pp;

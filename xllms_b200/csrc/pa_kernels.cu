@@ -181,6 +181,11 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
     pa_tma_mma_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const Params p) {
   using C = FastCfg<D, NT, STAGES, NWC>;
+  // Page j goes to stage j % STAGES and to consumer warp j % NWC. The parity
+  // waits below are only sound when every stage always belongs to the same
+  // warp: otherwise a warp could test a stage one phase early, see the parity
+  // of the previous (completed) phase and arrive on the barrier out of turn.
+  static_assert(STAGES % NWC == 0, "ring stages must be a multiple of the consumer warps");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -544,11 +549,24 @@ cudaError_t launch_generic_typed(const Params& p, cudaStream_t st) {
   return launch_generic_dpl<T, 8>(p, st);
 }
 
+// Ring depth of the TMA pipeline (pages in flight per CTA) and consumer warps
+// per CTA. Measured on B200 at config 2: a 4-page ring with 2 consumer warps
+// (~35 KB of shared memory, 6 CTAs per SM) streams faster than deeper rings
+// with more warps per CTA; more resident CTAs hide page latency better than a
+// deeper ring per CTA. A build may override either for tuning sweeps.
+#ifndef XPA_RING_PAGES
+#define XPA_RING_PAGES 4
+#endif
+#ifndef XPA_CONSUMER_WARPS
+#define XPA_CONSUMER_WARPS 2
+#endif
+
 template <int D, int NT>
 cudaError_t launch_fast_t(const CUtensorMap& tk, const CUtensorMap& tv, const Params& p,
                           cudaStream_t st) {
-  constexpr int STAGES = (D == 256) ? 4 : 8;
-  constexpr int NWC = 4;
+  constexpr int STAGES = (D == 256) ? (XPA_RING_PAGES / 2 > 1 ? XPA_RING_PAGES / 2 : 2)
+                                    : XPA_RING_PAGES;
+  constexpr int NWC = XPA_CONSUMER_WARPS;
   using C = FastCfg<D, NT, STAGES, NWC>;
   auto kern = pa_tma_mma_kernel<D, NT, STAGES, NWC>;
   // The attribute is per function and device; setting it every call costs
