@@ -122,7 +122,8 @@ const char *nxt_paged_attention_strerror(int code);
  *                     or NULL for the library's per-device status word.
  * Returns NXT_PA_OK once the kernels are enqueued, else a negative code.
  * Partials of one call live in the workspace until the call's kernels finish,
- * so concurrent calls need distinct workspaces. */
+ * so concurrent calls need distinct workspaces. A call whose sequences span
+ * more than one partition launches two kernels (attention, then the merge). */
 int nxt_paged_attention_ex(
     void *out, const void *query,
     const void *key_cache, const void *value_cache,
@@ -193,6 +194,14 @@ int nxt_paged_attention_noalloc(
     int64_t num_blocks,
     int *device_status,
     nxt_stream_t stream);
+
+/* extension — failure-detection testing: sets the bound on every pipeline
+ * wait inside the kernels launched by later calls from this host thread
+ * (default 1 s; each wait gives up after that much %globaltimer time, raises
+ * NXT_PA_DEV_TIMEOUT and the kernel winds down, letting its own in-flight
+ * copies land under a separate 1 s bound). Returns the previous budget. A
+ * tiny budget makes the waits run out on purpose without faulting the GPU. */
+uint64_t nxt_paged_attention_set_wait_budget_ns(uint64_t budget_ns);
 
 /* extension — instrumentation for timing the attention kernel alone. The next
  * call made by this host thread records `before` on its stream immediately

@@ -12,7 +12,7 @@ from xllms_b200 import operator_api as PA
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 INCLUDE = os.path.join(ROOT, "include")
-DECL = re.compile(r"^\s*(?:void|int|size_t|const\s+char)\s*\*?\s*(nxt_\w+)\s*\(", re.M)
+DECL = re.compile(r"^\s*(?:void|int|size_t|uint64_t|const\s+char)\s*\*?\s*(nxt_\w+)\s*\(", re.M)
 
 
 def declared(header):

@@ -55,6 +55,7 @@ SIGNATURES = {
          _VP, _VP],
     ),
     "nxt_paged_attention_profile_next": (_I, [_VP, _VP]),
+    "nxt_paged_attention_set_wait_budget_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "nxt_paged_attention_device_info": (
         _I, [ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.c_char_p, _I]),
 }

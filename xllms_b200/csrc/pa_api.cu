@@ -22,6 +22,7 @@ thread_local cudaEvent_t g_prof_before = nullptr;  // one-shot timing events
 thread_local cudaEvent_t g_prof_after = nullptr;
 
 constexpr unsigned long long kWaitBudgetNs = 1000000000ull;  // 1 s per pipeline wait
+thread_local unsigned long long g_wait_budget_ns = kWaitBudgetNs;
 constexpr int kMaxDevices = 64;
 
 std::mutex g_mu;
@@ -34,7 +35,7 @@ struct DeviceState {
 DeviceState g_dev[kMaxDevices];
 
 struct Workspace {
-  void* ptr = nullptr;
+  void* ptr = nullptr;  // split-context partials
   size_t bytes = 0;
 };
 // Keyed by (device, stream) so calls on different streams never share partials.
@@ -239,7 +240,7 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   p.kv_block_stride = kbs;
   p.kv_head_stride = khs;
   p.num_blocks = num_blocks;
-  p.timeout_ns = kWaitBudgetNs;
+  p.timeout_ns = g_wait_budget_ns;
   p.B = B;
   p.Hq = Hq;
   p.Hkv = Hkv;
@@ -410,6 +411,12 @@ int nxt_paged_attention_release_workspaces(void) {
   }
   if (have_prev) cudaSetDevice(prev);
   return rc;
+}
+
+uint64_t nxt_paged_attention_set_wait_budget_ns(uint64_t budget_ns) {
+  const uint64_t prev = g_wait_budget_ns;
+  g_wait_budget_ns = budget_ns;
+  return prev;
 }
 
 int nxt_paged_attention_profile_next(void* before, void* after) {

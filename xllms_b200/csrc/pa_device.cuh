@@ -28,7 +28,7 @@ struct Params {
   long long kv_block_stride;
   long long kv_head_stride;
   long long num_blocks;  // <= 0: unknown, no upper bound check
-  unsigned long long timeout_ns;  // bound on every pipeline wait
+  unsigned long long timeout_ns;  // bound on every pipeline wait (not on the drain)
   int B, Hq, Hkv, D, GS;
   int max_blocks, block_size;
   int part_pages, max_parts;
@@ -132,14 +132,33 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t parity)
   return ok;
 }
 
+__device__ __forceinline__ uint32_t mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok;
+}
+
 // Waits for the phase with the given parity to complete, for at most
-// budget_ns of wall time. Returns false when the budget ran out.
+// budget_ns of %globaltimer time. Returns false when the budget ran out.
+// The first probe does not block (test_wait), and the budget is checked
+// before the first blocking probe (try_wait may suspend the thread in
+// hardware) and then before every XPA_WAIT_CHECK_EVERY-th one, so a zero
+// budget gives up as soon as the phase is found incomplete.
+#ifndef XPA_WAIT_CHECK_EVERY
+#define XPA_WAIT_CHECK_EVERY 8
+#endif
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t budget_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
+  for (uint32_t it = 0;; ++it) {
+    if (it % XPA_WAIT_CHECK_EVERY == 0 && globaltimer_ns() - t0 >= budget_ns) return false;
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0u && globaltimer_ns() - t0 > budget_ns) return false;
   }
 }
 
@@ -151,6 +170,18 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ── programmatic dependent launch ───────────────────────────────────────
+// Lets a kernel launched after this one with programmatic stream
+// serialisation start once every CTA of this grid has issued the trigger.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Waits until the preceding grid has completed and its memory is visible
+// (a no-op when the launch did not use programmatic serialisation).
+__device__ __forceinline__ void pdl_wait_primary() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // ── TMA (tensor, tiled, no multicast) ───────────────────────────────────
@@ -223,5 +254,111 @@ template <>
 __device__ __forceinline__ float from_float<float>(float x) { return x; }
 template <>
 __device__ __forceinline__ __half from_float<__half>(float x) { return __float2half_rn(x); }
+
+
+// ── split-context merge ─────────────────────────────────────────────────
+struct CtaSync {
+  __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
+// Log-sum-exp merge of the partials of one (b, q head) row into out:
+//   M = max_p m_p,  w_p = 2^(m_p - M),  out = sum_p w_p o_p / sum_p w_p l_p.
+// Run by `nthr` threads (index tid) that synchronise with sync(); `sm` is
+// shared scratch of cap + 34 floats (weights of the first `cap` partitions,
+// the rest recomputed). Partials were written by other CTAs of the same
+// launch, so they are read through L2 (ld.global.cg).
+template <typename T, typename Sync>
+__device__ __forceinline__ void merge_row(const Params& p, long long row, int nparts, int tid,
+                                          int nthr, float* sm, int cap, Sync sync) {
+  float* red = sm + cap;
+  const float* ml = p.part_ml + row * p.max_parts * 2;
+  const int lane = tid & 31, wid = tid >> 5, nw = (nthr + 31) >> 5;
+  float mx = -INFINITY;
+  for (int i = tid; i < nparts; i += nthr) mx = fmaxf(mx, __ldcg(ml + 2 * i));
+  mx = warp_max(mx);
+  if (lane == 0) red[wid] = mx;
+  sync();
+  float M = -INFINITY;
+  for (int w = 0; w < nw; ++w) M = fmaxf(M, red[w]);
+  float den = 0.f;
+  for (int i = tid; i < nparts; i += nthr) {
+    const float mp = __ldcg(ml + 2 * i);
+    const float wt = (M == -INFINITY || mp == -INFINITY) ? 0.f : ex2(mp - M);
+    if (i < cap) sm[i] = wt;
+    den = fmaf(wt, __ldcg(ml + 2 * i + 1), den);
+  }
+  den = warp_sum(den);
+  sync();  // every thread has read M from red[]
+  if (lane == 0) red[wid] = den;
+  sync();
+  float tot = 0.f;
+  for (int w = 0; w < nw; ++w) tot += red[w];
+  const float* po = p.part_o + row * p.max_parts * p.D;
+  T* out = static_cast<T*>(p.out) + row * p.D;
+  for (int d = tid; d < p.D; d += nthr) {
+    float acc = 0.f;
+    for (int i = 0; i < nparts; ++i) {
+      float wt;
+      if (i < cap) {
+        wt = sm[i];
+      } else {
+        const float mp = __ldcg(ml + 2 * i);
+        wt = (M == -INFINITY || mp == -INFINITY) ? 0.f : ex2(mp - M);
+      }
+      acc = fmaf(wt, __ldcg(po + (long long)i * p.D + d), acc);
+    }
+    out[d] = from_float<T>(tot > 0.f ? acc / tot : 0.f);
+  }
+  sync();  // sm and red are reused by the next row
+}
+
+// Merges the partials of the GS query heads (rows row0 .. row0+GS-1) of one
+// (sequence, KV head) at once: every
+// (head, partition) max and sum is staged in shared memory in one pass, the
+// weights of all heads are formed in parallel, and each output element then
+// needs nparts independent loads. Falls back to merge_row per head when the
+// staging does not fit in `cap` floats.
+template <typename T, typename Sync>
+__device__ __forceinline__ void merge_group(const Params& p, long long row0, int np, int tid,
+                                            int nthr, float* sm, int cap, Sync sync) {
+  const int GS = p.GS, D = p.D;
+  if (2 * GS * np + GS > cap) {
+    for (int h = 0; h < GS; ++h) merge_row<T>(p, row0 + h, np, tid, nthr, sm, cap, sync);
+    return;
+  }
+  float* sw = sm;                // [GS][np]: maxima, then weights
+  float* sl = sm + GS * np;      // [GS][np]: sums
+  float* sinv = sl + GS * np;    // [GS]: 1 / merged sum
+  for (int e = tid; e < GS * np; e += nthr) {
+    const int h = e / np, i = e - h * np;
+    const float* ml = p.part_ml + ((row0 + h) * p.max_parts + i) * 2;
+    sw[e] = __ldcg(ml);
+    sl[e] = __ldcg(ml + 1);
+  }
+  sync();
+  for (int h = tid; h < GS; h += nthr) {
+    float M = -INFINITY;
+    for (int i = 0; i < np; ++i) M = fmaxf(M, sw[h * np + i]);
+    float den = 0.f;
+    for (int i = 0; i < np; ++i) {
+      const float m = sw[h * np + i];
+      const float wt = (M == -INFINITY || m == -INFINITY) ? 0.f : ex2(m - M);
+      sw[h * np + i] = wt;
+      den = fmaf(wt, sl[h * np + i], den);
+    }
+    sinv[h] = den > 0.f ? 1.f / den : 0.f;
+  }
+  sync();
+  T* out = static_cast<T*>(p.out);
+  for (int e = tid; e < GS * D; e += nthr) {
+    const int h = e / D, d = e - h * D;
+    const float* po = p.part_o + (row0 + h) * p.max_parts * D + d;
+    const float* w = sw + h * np;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < np; ++i) acc = fmaf(w[i], __ldcg(po + (long long)i * D), acc);
+    out[(row0 + h) * D + d] = from_float<T>(acc * sinv[h]);
+  }
+}
 
 }  // namespace xpa

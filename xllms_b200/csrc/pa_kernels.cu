@@ -5,8 +5,10 @@
 // of the sequence's block-table row. A sequence that fits in one partition is
 // finished in place (normalised output written directly); longer ones write
 // per-partition partials (running max m, sum l, unnormalised o) that
-// pa_reduce_kernel merges by log-sum-exp. Scores are kept in the exp2 domain
-// (scale * log2 e folded into the score), which is the same softmax.
+// pa_reduce_kernel merges by log-sum-exp, launched as a programmatic
+// dependent of the attention kernel so its launch overlaps that kernel's tail.
+// Scores are kept in the exp2 domain (scale * log2 e folded into the score),
+// which is the same softmax.
 //
 // Reference semantics followed: GQA mapping kv = h / (Hq/Hkv)
 // (examples/text_gen.c:1285), max-subtracted softmax and o = sum w*v
@@ -33,6 +35,7 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
   __shared__ float sm_m[NW][HG];
   __shared__ float sm_l[NW][HG];
 
+  pdl_launch_dependents();
   Item it;
   const ItemKind kind = decode_item(p, blockIdx.x, it);
   if (kind == kItemNone) return;
@@ -163,6 +166,9 @@ __device__ __forceinline__ uint32_t tile_off(int tok, int chunk) {
   return (uint32_t)((chunk >> 3) * 2048 + tok * 128 + (((chunk & 7) ^ (tok & 7)) << 4));
 }
 
+// Bound on the producer's wait for its own in-flight copies after a timeout.
+constexpr uint64_t kDrainBudgetNs = 1000000000ull;
+
 template <int D, int NT, int STAGES, int NWC>
 struct FastCfg {
   static constexpr int kTile = 16 * D * 2;     // bytes of one K (or V) page
@@ -191,6 +197,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   int* meta = reinterpret_cast<int*>(smem + C::kBarOff + STAGES * 16);
 
+  pdl_launch_dependents();
   Item it;
   const ItemKind kind = decode_item(p, blockIdx.x, it);
   if (kind == kItemNone) return;
@@ -262,9 +269,10 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
       if (!ok) break;
     }
     if (!ok && lane == 0) {
-      // Let copies already in flight land before the CTA can retire.
+      // Let copies already in flight land before the CTA can retire. The
+      // drain has its own bound, independent of the pipeline-wait budget.
       for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
-        (void)mbar_wait(bar_full + 8 * (j % STAGES), (j / STAGES) & 1, budget);
+        (void)mbar_wait(bar_full + 8 * (j % STAGES), (j / STAGES) & 1, kDrainBudgetNs);
     }
     return;
   }
@@ -466,51 +474,39 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
 }
 
 // ════════════════════════════════════════════════════════════════════════
-// Log-sum-exp reduce of split-context partials: one CTA per (b, q head).
+// Log-sum-exp reduce of split-context partials:
 //   M = max_p m_p,  w_p = 2^(m_p - M),  out = sum_p w_p o_p / sum_p w_p l_p
+// XPA_REDUCE_GROUPED 0: one CTA per (b, q head) row (merge_row);
+//                    1: one CTA per (b, KV head), its GS rows together.
 // ════════════════════════════════════════════════════════════════════════
+#ifndef XPA_REDUCE_GROUPED
+#define XPA_REDUCE_GROUPED 0
+#endif
+#ifndef XPA_REDUCE_PDL
+#define XPA_REDUCE_PDL 1
+#endif
 template <typename T>
-__global__ void __launch_bounds__(128) pa_reduce_kernel(const Params p) {
-  extern __shared__ float sm_w[];  // [max_parts]
-  __shared__ float sh_M, sh_den;
+__global__ void __launch_bounds__(128) pa_reduce_kernel(const Params p, int cap) {
+  extern __shared__ float sm_w[];  // [cap + 34]
+#if XPA_REDUCE_GROUPED
+  const int b = blockIdx.x / p.Hkv, kvh = blockIdx.x % p.Hkv;
+#else
   const long long row = blockIdx.x;
   const int b = (int)(row / p.Hq);
+#endif
   int L = __ldg(p.seq_lens + b);
-  const long long cap = (long long)p.max_blocks * p.block_size;
-  L = L < 0 ? 0 : ((long long)L > cap ? (int)cap : L);
+  const long long lim = (long long)p.max_blocks * p.block_size;
+  L = L < 0 ? 0 : ((long long)L > lim ? (int)lim : L);
   const int npages = (L + p.block_size - 1) / p.block_size;
   const int nparts = (npages + p.part_pages - 1) / p.part_pages;
   if (nparts <= 1) return;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float* ml = p.part_ml + row * p.max_parts * 2;
-  if (warp == 0) {
-    float M = -INFINITY;
-    for (int i = lane; i < nparts; i += 32) M = fmaxf(M, ml[2 * i]);
-    M = warp_max(M);
-    if (lane == 0) sh_M = M;
-  }
-  __syncthreads();
-  const float M = sh_M;
-  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
-    const float mp = ml[2 * i];
-    sm_w[i] = (M == -INFINITY || mp == -INFINITY) ? 0.f : ex2(mp - M);
-  }
-  __syncthreads();
-  if (warp == 0) {
-    float den = 0.f;
-    for (int i = lane; i < nparts; i += 32) den = fmaf(sm_w[i], ml[2 * i + 1], den);
-    den = warp_sum(den);
-    if (lane == 0) sh_den = den;
-  }
-  __syncthreads();
-  const float den = sh_den;
-  const float* po = p.part_o + row * p.max_parts * p.D;
-  T* out = static_cast<T*>(p.out) + row * p.D;
-  for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
-    float acc = 0.f;
-    for (int i = 0; i < nparts; ++i) acc = fmaf(sm_w[i], po[(long long)i * p.D + d], acc);
-    out[d] = from_float<T>(den > 0.f ? acc / den : 0.f);
-  }
+  pdl_wait_primary();  // the partials are the attention kernel's output
+#if XPA_REDUCE_GROUPED
+  merge_group<T>(p, (long long)b * p.Hq + (long long)kvh * p.GS, nparts, threadIdx.x,
+                 blockDim.x, sm_w, cap, CtaSync());
+#else
+  merge_row<T>(p, row, nparts, threadIdx.x, blockDim.x, sm_w, cap, CtaSync());
+#endif
 }
 
 // ════════════════════════════════════════════════════════════════════════
@@ -606,14 +602,28 @@ cudaError_t launch_fast(const CUtensorMap& tk, const CUtensorMap& tv, const Para
 }
 
 cudaError_t launch_reduce(const Params& p, int dtype_size, cudaStream_t st) {
-  const long long grid = (long long)p.B * p.Hq;
-  const size_t smem = (size_t)p.max_parts * sizeof(float);
-  if (smem > 48 * 1024) return cudaErrorInvalidValue;
-  if (dtype_size == 4)
-    pa_reduce_kernel<float><<<(unsigned)grid, 128, smem, st>>>(p);
-  else
-    pa_reduce_kernel<__half><<<(unsigned)grid, 128, smem, st>>>(p);
-  return cudaGetLastError();
+#if XPA_REDUCE_GROUPED
+  // The (head, partition) maxima, sums and weights, when they fit in 48 KB
+  // (else merge_group falls back to merging row by row).
+  const long long want = 2LL * p.GS * p.max_parts + p.GS;
+  const unsigned grid = (unsigned)((long long)p.B * p.Hkv);
+#else
+  const long long want = p.max_parts;  // the row's partition weights
+  const unsigned grid = (unsigned)((long long)p.B * p.Hq);
+#endif
+  const int cap = (int)(want < 12 * 1024 - 34 ? want : 12 * 1024 - 34);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = (size_t)(cap + 34) * sizeof(float);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = XPA_REDUCE_PDL ? 1 : 0;
+  if (dtype_size == 4) return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<float>, p, cap);
+  return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<__half>, p, cap);
 }
 
 }  // namespace xpa
