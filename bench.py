@@ -50,6 +50,10 @@ def parse_args():
                     help="wall-time budget of the cpu_baseline leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the e2e leg (profiling runs)")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: fused = kernels store each rank's heads into every GPU's "
+                         "buffer over NVLink (nxt_paged_attention_sharded); nccl = NCCL "
+                         "all-gather + head interleave")
     ap.add_argument("--seqs", type=int, default=0,
                     help="sequences per GPU for c2/c4/c5 (default: the BASELINE size); smaller "
                          "values make the small cases the ncu captures run on")
@@ -251,8 +255,13 @@ def run_ours(args, rank, world, local_rank):
     q, k, v = batch.values_torch(dev)
     bt, sl = batch.tables_torch(dev)
     out = torch.empty_like(q)
-    gathered = full = None
-    if world > 1:
+    gathered = full = fg = None
+    fused = world > 1 and args.gather == "fused"
+    if fused:
+        fg = sharding.FusedHeadGather(batch.num_seqs, batch.total_heads, batch.head_size,
+                                      batch.dtype_size, world, rank, sharding.torch_exchange(),
+                                      dev)
+    elif world > 1:
         gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
         full = torch.empty((batch.num_seqs, batch.total_heads, batch.head_size),
                            dtype=out.dtype, device=dev)
@@ -263,9 +272,13 @@ def run_ours(args, rank, world, local_rank):
     split = PA.workspace_size(batch.num_seqs, batch.num_heads, batch.head_size,
                               batch.num_kv_heads, batch.max_blocks, batch.block_size,
                               batch.dtype_size) > 0
-    launches_per_step = 1 + (1 if split else 0)  # attention kernel (+ split-context merge)
+    # attention kernel (+ split-context merge) (+ the fused gather's barrier)
+    launches_per_step = 1 + (1 if split else 0) + (1 if fused else 0)
 
     def step():
+        if fused:
+            fg.run(q, k, v, bt, sl, batch.scale, batch.num_blocks)
+            return
         PA.paged_attention(q, k, v, bt, sl, out=out, num_blocks=batch.num_blocks)
         if world > 1:
             sharding.gather_heads(out, gathered)
@@ -296,7 +309,8 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     clocks.stop()
     t_step = start.elapsed_time(stop) / K
-    resident = (full if world > 1 else out).clone()  # output of the device-resident run
+    # output of the device-resident run
+    resident = (fg.output(fg.step) if fused else (full if world > 1 else out)).clone()
 
     # Timed region 2: K steps with events recorded by the library right around
     # the attention kernel -> its own mean duration for the roofline. (Kept
@@ -318,6 +332,8 @@ def run_ours(args, rank, world, local_rank):
 
     # ── e2e through the backend plugin (C ABI) with host buffers ───────────
     if args.no_e2e:
+        if fg is not None:
+            fg.close(dist.barrier)
         return _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, None,
                        clocks, None, q, k, v, 0, 0, dev)
     plugin = PA.CudaBackendPlugin()
@@ -334,13 +350,19 @@ def run_ours(args, rank, world, local_rank):
     bt_d = stage_d[nq:nq + nbt].view(torch.int32).view(bt.shape)
     sl_d = stage_d[nq + nbt:].view(torch.int32).view(sl.shape)
     out_d = torch.empty_like(out)
-    res = full if world > 1 else out_d
-    out_h = torch.empty(res.shape, dtype=res.dtype).pin_memory()
+    res = full if (world > 1 and not fused) else out_d
+    out_h = torch.empty((batch.num_seqs, batch.total_heads, batch.head_size),
+                        dtype=out.dtype).pin_memory()
     pa_in = PA.make_input(q_d, k, v, bt_d, sl_d, scale=batch.scale,
                           stream=torch.cuda.current_stream())
 
     def e2e_step():
         stage_d.copy_(stage_h, non_blocking=True)
+        if fused:
+            # the C-ABI sharded entry point (the plugin descriptor has no shard fields)
+            out_h.copy_(fg.run(q_d, k, v, bt_d, sl_d, batch.scale, batch.num_blocks),
+                        non_blocking=True)
+            return
         if plugin.run(pa_in, out_d) != 0:
             raise SystemExit("nxt_backend_run failed")
         if world > 1:
@@ -364,6 +386,8 @@ def run_ours(args, rank, world, local_rank):
     if not torch.equal(out_h.to(dev), resident):
         raise SystemExit("e2e output differs from the device-resident run")
     plugin.close()
+    if fg is not None:
+        fg.close(dist.barrier)
     h2d = stage_h.numel()
     d2h = out_h.numel() * out_h.element_size()
     return _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t_e2e,
@@ -426,7 +450,10 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
             "max_blocks_per_seq": batch.max_blocks,
             "context_tokens": batch.context_tokens(),
             "parallelism": "single GPU" if world == 1 else
-                           f"KV-head sharding x{world} + NCCL all-gather of outputs",
+                           (f"KV-head sharding x{world}, output gather fused into the kernels "
+                            "(NVLink peer stores + bounded cross-GPU barrier)"
+                            if args.gather == "fused" else
+                            f"KV-head sharding x{world} + NCCL all-gather of outputs"),
             "l2": f"no flush: each step reads {tot_kv / world / 1e9:.2f} GB of KV per GPU "
                   f"(> {L2_BYTES >> 20} MB L2)",
             "path": {1: "tma_mma", 2: "generic"}.get(path, "none"),

@@ -203,6 +203,59 @@ int nxt_paged_attention_noalloc(
  * tiny budget makes the waits run out on purpose without faulting the GPU. */
 uint64_t nxt_paged_attention_set_wait_budget_ns(uint64_t budget_ns);
 
+/* ── extension: KV-head sharding with the output all-gather fused in ────
+ * For P GPUs of one box, one process or thread per GPU. Rank r owns KV
+ * heads [r*Hkv/P, (r+1)*Hkv/P) with their query heads (head_offset =
+ * r*Hq/P), its own page pools and block tables. Every rank allocates one
+ * gather buffer (nxt_pa_peer_alloc: 2 halves of [num_seqs][total_heads]
+ * [head_size] elements, then world_size uint64 flags), shares its IPC handle
+ * with the others (any host-side channel) and opens theirs (nxt_pa_peer_open).
+ * nxt_paged_attention_sharded then writes this rank's output heads directly
+ * into every rank's buffer over NVLink peer stores (no collective library,
+ * no multicast) and ends with a bounded cross-GPU barrier: when its stream
+ * reaches the end of step s, half (s & 1) of this rank's buffer holds the
+ * whole [num_seqs][total_heads][head_size] output of step s from all ranks.
+ * Consume that half before enqueueing step s + 2 on the same stream. A peer
+ * that does not arrive within the wait budget raises NXT_PA_DEV_TIMEOUT. */
+#define NXT_PA_MAX_PEERS 8
+#define NXT_PA_IPC_HANDLE_BYTES 64
+
+typedef struct {
+    int       world_size;                    /* P, 1..NXT_PA_MAX_PEERS        */
+    int       rank;                          /* this GPU's rank               */
+    int       total_heads;                   /* query heads over all ranks    */
+    int       head_offset;                   /* first query head of this rank */
+    void     *peer_out[NXT_PA_MAX_PEERS];    /* rank r's gather buffer (opened) */
+    uint64_t *peer_flags[NXT_PA_MAX_PEERS];  /* rank r's flag array (opened)  */
+} NxtPaShard;
+
+/* Allocates `bytes` of zero-filled device memory on the current device and
+ * writes its IPC handle (NXT_PA_IPC_HANDLE_BYTES) to `ipc_handle`. */
+int nxt_pa_peer_alloc(size_t bytes, void **dev_ptr, void *ipc_handle);
+/* Maps another process's buffer (from its IPC handle) on the current device. */
+int nxt_pa_peer_open(const void *ipc_handle, void **dev_ptr);
+/* Unmaps a buffer opened with nxt_pa_peer_open. */
+int nxt_pa_peer_close(void *dev_ptr);
+/* Frees a buffer from nxt_pa_peer_alloc (after every peer has closed it). */
+int nxt_pa_peer_free(void *dev_ptr);
+
+/* Sharded decode attention for step `step` (1, 2, 3, ...): the arguments of
+ * nxt_paged_attention_ex for this rank's heads (num_heads, num_kv_heads are
+ * this rank's counts), without `out` and the workspace. */
+int nxt_paged_attention_sharded(
+    const NxtPaShard *shard, uint64_t step,
+    const void *query,
+    const void *key_cache, const void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq,
+    int block_size, int dtype_size,
+    int64_t kv_block_stride, int64_t kv_head_stride,
+    int64_t num_blocks,
+    int *device_status,
+    nxt_stream_t stream);
+
 /* extension — instrumentation for timing the attention kernel alone. The next
  * call made by this host thread records `before` on its stream immediately
  * before the main attention kernel and `after` immediately after it (ahead of

@@ -141,3 +141,9 @@ int main(void) {
     subprocess.run([cc, "-std=c11", "-I", INCLUDE, str(src), "-o", str(exe)], check=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
     assert out == ["88", "112", "120", "80", "88"]
+
+
+def test_shard_descriptor_layout():
+    from xllms_b200 import sharding as S
+    assert ctypes.sizeof(S.NxtPaShard) == 144
+    assert S.NxtPaShard.peer_out.offset == 16 and S.NxtPaShard.peer_flags.offset == 80

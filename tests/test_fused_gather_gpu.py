@@ -1,0 +1,126 @@
+"""Fused head gather (nxt_paged_attention_sharded) on one GPU.
+
+Two ranks are emulated on one GPU: each rank's launch stores its heads into
+both ranks' gather buffers. The end-of-step barrier waits for every rank's
+signal; here those signals are set on the host before the launches, so no
+launch ever waits on another launch on the same GPU. With one signal left
+unset (a flag that nothing sets) the barrier's bounded wait must run out and
+report NXT_PA_DEV_TIMEOUT, leaving the context usable."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from _helpers import check_close
+from oracle import oracle as O
+from xllms_b200 import _native
+from xllms_b200 import sharding as S
+from xllms_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _buffers(lib, B, H, D, es, world):
+    half = B * H * D * es
+    flags_off = (2 * half + 255) // 256 * 256
+    bufs = []
+    for _ in range(world):
+        p = ctypes.c_void_p()
+        h = (ctypes.c_char * _native.NXT_PA_IPC_HANDLE_BYTES)()
+        assert lib.nxt_pa_peer_alloc(flags_off + 8 * world, ctypes.byref(p), h) == 0
+        bufs.append(p.value)
+    return bufs, half, flags_off
+
+
+def _shards(bufs, flags_off, H, world):
+    out = []
+    for r in range(world):
+        sh = S.NxtPaShard()
+        sh.world_size, sh.rank, sh.total_heads, sh.head_offset = world, r, H, r * (H // world)
+        for p in range(world):
+            sh.peer_out[p] = bufs[p]
+            sh.peer_flags[p] = bufs[p] + flags_off
+        out.append(sh)
+    return out
+
+
+def _flags(ptr, world, dev):
+    import torch
+    return torch.as_tensor(S._DeviceArray(ptr, (world,), "<i8"), device=dev)
+
+
+def _call(lib, sh, step, b, qs, ks, vs, bt, sl, status):
+    return lib.nxt_paged_attention_sharded(
+        ctypes.byref(sh), step, qs.data_ptr(), ks.data_ptr(), vs.data_ptr(), bt.data_ptr(),
+        sl.data_ptr(), b.num_seqs, qs.shape[1], b.head_size, ks.shape[1], b.scale, b.max_blocks,
+        16, 2, ks.shape[1] * 16 * b.head_size, 16 * b.head_size, b.num_blocks,
+        status.data_ptr(), None)
+
+
+def _setup(cuda):
+    import torch
+    b = W.make_batch("fg", [1, 700, 2100, 0, 5000, 16], 32, 8, 128, "f16", 81, value_std=0.5)
+    q, k, v = b.values_numpy()
+    ref = O.attention(q, k, v, b.block_tables, b.seq_lens, b.num_kv_heads, b.scale)
+    bt, sl = b.tables_torch(cuda)
+    ranks = []
+    for r in range(WORLD):
+        qs, ks, vs = S.shard_heads(q, k, v, b.num_kv_heads, WORLD, r)
+        ranks.append(tuple(torch.from_numpy(x).to(cuda) for x in (qs, ks, vs)))
+    return b, ref, bt, sl, ranks
+
+
+def test_emulated_ranks_gather_into_every_buffer(cuda):
+    import torch
+    lib = _native.xpa()
+    b, ref, bt, sl, ranks = _setup(cuda)
+    bufs, half, flags_off = _buffers(lib, b.num_seqs, 32, 128, 2, WORLD)
+    shards = _shards(bufs, flags_off, 32, WORLD)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    try:
+        for step in (1, 2, 3):
+            for r in range(WORLD):
+                _flags(bufs[r] + flags_off, WORLD, cuda).fill_(step)
+            for r in range(WORLD):
+                assert _call(lib, shards[r], step, b, *ranks[r], bt, sl, status) == 0
+            torch.cuda.synchronize()
+            for r in range(WORLD):
+                view = torch.as_tensor(S._DeviceArray(bufs[r] + (step & 1) * half,
+                                                      (b.num_seqs, 32, 128), "<f2"), device=cuda)
+                check_close(view, ref, what=f"step {step} buffer {r}")
+        assert int(status.item()) == 0
+    finally:
+        torch.cuda.synchronize()
+        for p in bufs:
+            lib.nxt_pa_peer_free(p)
+
+
+def test_missing_peer_signal_times_out(cuda):
+    import torch
+    lib = _native.xpa()
+    b, ref, bt, sl, ranks = _setup(cuda)
+    bufs, half, flags_off = _buffers(lib, b.num_seqs, 32, 128, 2, WORLD)
+    shards = _shards(bufs, flags_off, 32, WORLD)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    prev = lib.nxt_paged_attention_set_wait_budget_ns(20_000_000)  # 20 ms
+    try:
+        # rank 1 never runs: its signal in rank 0's flag array stays unset
+        assert _call(lib, shards[0], 1, b, *ranks[0], bt, sl, status) == 0
+        torch.cuda.synchronize()
+        assert int(status.item()) & _native.NXT_PA_DEV_TIMEOUT
+    finally:
+        lib.nxt_paged_attention_set_wait_budget_ns(prev)
+    # the context is still usable: a complete step succeeds
+    status.zero_()
+    for r in range(WORLD):
+        _flags(bufs[r] + flags_off, WORLD, cuda).fill_(2)
+    for r in range(WORLD):
+        assert _call(lib, shards[r], 2, b, *ranks[r], bt, sl, status) == 0
+    torch.cuda.synchronize()
+    view = torch.as_tensor(S._DeviceArray(bufs[0], (b.num_seqs, 32, 128), "<f2"), device=cuda)
+    check_close(view, ref, what="after timeout")
+    assert int(status.item()) == 0
+    for p in bufs:
+        lib.nxt_pa_peer_free(p)

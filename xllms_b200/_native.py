@@ -29,6 +29,8 @@ NXT_PA_DEV_SEQ_CLAMPED = 0x4
 NXT_PA_PATH_NONE = 0
 NXT_PA_PATH_TMA_MMA = 1
 NXT_PA_PATH_GENERIC = 2
+NXT_PA_MAX_PEERS = 8
+NXT_PA_IPC_HANDLE_BYTES = 64
 
 # Every function include/operator_api.h declares, with its ctypes signature.
 _VP, _CVP, _IP = ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p
@@ -55,6 +57,15 @@ SIGNATURES = {
          _VP, _VP],
     ),
     "nxt_paged_attention_profile_next": (_I, [_VP, _VP]),
+    "nxt_pa_peer_alloc": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p), _VP]),
+    "nxt_pa_peer_open": (_I, [_VP, ctypes.POINTER(ctypes.c_void_p)]),
+    "nxt_pa_peer_close": (_I, [_VP]),
+    "nxt_pa_peer_free": (_I, [_VP]),
+    "nxt_paged_attention_sharded": (
+        _I,
+        [_VP, ctypes.c_uint64, _CVP, _CVP, _CVP, _IP, _IP, _I, _I, _I, _I, _F, _I, _I, _I, _I64,
+         _I64, _I64, _VP, _VP],
+    ),
     "nxt_paged_attention_set_wait_budget_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "nxt_paged_attention_device_info": (
         _I, [ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.c_char_p, _I]),

@@ -190,7 +190,17 @@ namespace {
 int run(void* out, const void* q, const void* k, const void* v, const int* bt, const int* sl,
         int B, int Hq, int D, int Hkv, float scale, int max_blocks, int bs, int ds,
         long long kbs, long long khs, long long num_blocks, void* ws, size_t ws_bytes,
-        int* dev_status, cudaStream_t st) {
+        int* dev_status, cudaStream_t st, const NxtPaShard* shard = nullptr,
+        uint64_t step = 0) {
+  if (shard) {
+    if (shard->world_size < 1 || shard->world_size > NXT_PA_MAX_PEERS || shard->rank < 0 ||
+        shard->rank >= shard->world_size || step == 0 || shard->head_offset < 0 ||
+        (long long)shard->head_offset + Hq > shard->total_heads)
+      return NXT_PA_EINVAL;
+    for (int r = 0; r < shard->world_size; ++r)
+      if (!shard->peer_out[r] || !shard->peer_flags[r]) return NXT_PA_EINVAL;
+    out = shard->peer_out[shard->rank];
+  }
   int rc = check_args(out, q, k, v, bt, sl, B, Hq, D, Hkv, max_blocks, bs, ds, kbs, khs);
   if (rc != NXT_PA_OK || B == 0) return rc;
 
@@ -251,6 +261,13 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   p.part_pages = pl.part_pages;
   p.max_parts = pl.max_parts;
   p.scale_log2 = scale * 1.4426950408889634f;
+  if (shard) {
+    p.npeers = shard->world_size;
+    p.Hq_total = shard->total_heads;
+    p.head_offset = shard->head_offset;
+    p.peer_off = (long long)(step & 1) * B * shard->total_heads * D;
+    for (int r = 0; r < shard->world_size; ++r) p.peers[r] = shard->peer_out[r];
+  }
 
   cudaError_t e;
   CUtensorMap tk, tv;
@@ -267,6 +284,12 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   if (ev_b && cudaEventRecord(ev_b, st) != cudaSuccess) return NXT_PA_ECUDA;
   if (pl.max_parts > 1) {
     e = xpa::launch_reduce(p, ds, st);
+    if (e != cudaSuccess) return map_cuda(e);
+  }
+  if (shard) {
+    e = xpa::launch_peer_barrier(reinterpret_cast<void* const*>(shard->peer_flags),
+                                 shard->world_size, shard->rank, step, status, g_wait_budget_ns,
+                                 st);
     if (e != cudaSuccess) return map_cuda(e);
   }
   return NXT_PA_OK;
@@ -411,6 +434,55 @@ int nxt_paged_attention_release_workspaces(void) {
   }
   if (have_prev) cudaSetDevice(prev);
   return rc;
+}
+
+int nxt_pa_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle) {
+  if (!dev_ptr || !ipc_handle || bytes == 0) return NXT_PA_EINVAL;
+  static_assert(sizeof(cudaIpcMemHandle_t) == NXT_PA_IPC_HANDLE_BYTES, "IPC handle size");
+  void* ptr = nullptr;
+  if (cudaMalloc(&ptr, bytes) != cudaSuccess) return NXT_PA_ENOMEM;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(ptr, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) {
+    cudaFree(ptr);
+    return NXT_PA_ECUDA;
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *dev_ptr = ptr;
+  return NXT_PA_OK;
+}
+
+int nxt_pa_peer_open(const void* ipc_handle, void** dev_ptr) {
+  if (!dev_ptr || !ipc_handle) return NXT_PA_EINVAL;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  void* ptr = nullptr;
+  if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return NXT_PA_ECUDA;
+  *dev_ptr = ptr;
+  return NXT_PA_OK;
+}
+
+int nxt_pa_peer_close(void* dev_ptr) {
+  return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? NXT_PA_OK : NXT_PA_ECUDA;
+}
+
+int nxt_pa_peer_free(void* dev_ptr) {
+  return cudaFree(dev_ptr) == cudaSuccess ? NXT_PA_OK : NXT_PA_ECUDA;
+}
+
+int nxt_paged_attention_sharded(const NxtPaShard* shard, uint64_t step, const void* query,
+                                const void* key_cache, const void* value_cache,
+                                const int* block_tables, const int* seq_lens, int num_seqs,
+                                int num_heads, int head_size, int num_kv_heads, float scale,
+                                int max_num_blocks_per_seq, int block_size, int dtype_size,
+                                int64_t kv_block_stride, int64_t kv_head_stride,
+                                int64_t num_blocks, int* device_status, nxt_stream_t stream) {
+  if (!shard) return NXT_PA_EINVAL;
+  return run(nullptr, query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads,
+             head_size, num_kv_heads, scale, max_num_blocks_per_seq, block_size, dtype_size,
+             kv_block_stride, kv_head_stride, num_blocks, nullptr, 0, device_status,
+             static_cast<cudaStream_t>(stream), shard, step);
 }
 
 uint64_t nxt_paged_attention_set_wait_budget_ns(uint64_t budget_ns) {

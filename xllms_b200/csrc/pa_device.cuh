@@ -14,6 +14,8 @@ constexpr int kDevTimeout = 0x1;
 constexpr int kDevBadPage = 0x2;
 constexpr int kDevSeqClamped = 0x4;
 
+constexpr int kMaxPeers = 8;
+
 // Everything a launch needs besides the tensor maps. Strides are in elements.
 struct Params {
   void* out;              // [B][Hq][D]
@@ -33,6 +35,12 @@ struct Params {
   int max_blocks, block_size;
   int part_pages, max_parts;
   float scale_log2;  // scale * log2(e): scores live in the exp2 domain
+  // Fused head gather (KV-head sharding over GPUs): when npeers > 0 every
+  // output row (b, h) of this rank is stored into each peers[r] at element
+  // peer_off + (b * Hq_total + head_offset + h) * D, and `out` is unused.
+  int npeers, Hq_total, head_offset;
+  long long peer_off;
+  void* peers[kMaxPeers];
 };
 
 // One unit of work: context partition `part` of (sequence b, KV head kvh).
@@ -256,6 +264,25 @@ template <>
 __device__ __forceinline__ __half from_float<__half>(float x) { return __float2half_rn(x); }
 
 
+// Stores element d of output row `row` (= b * Hq + h, this launch's heads):
+// into `out`, or, with the fused head gather, into every rank's buffer. The
+// peer stores need no fence here: the gather barrier that publishes them runs
+// only after these grids have completed, and completion flushes their writes,
+// peer writes included (the guarantee CUDA's event-ordered P2P model uses).
+template <typename T>
+__device__ __forceinline__ void store_out(const Params& p, long long row, int d, float v) {
+  const T x = from_float<T>(v);
+  if (p.npeers == 0) {
+    static_cast<T*>(p.out)[row * p.D + d] = x;
+    return;
+  }
+  const long long b = row / p.Hq, h = row - b * p.Hq;
+  const long long off = p.peer_off + (b * p.Hq_total + p.head_offset + h) * p.D + d;
+#pragma unroll
+  for (int r = 0; r < kMaxPeers; ++r)
+    if (r < p.npeers) static_cast<T*>(p.peers[r])[off] = x;
+}
+
 // ── split-context merge ─────────────────────────────────────────────────
 struct CtaSync {
   __device__ __forceinline__ void operator()() const { __syncthreads(); }
@@ -294,7 +321,6 @@ __device__ __forceinline__ void merge_row(const Params& p, long long row, int np
   float tot = 0.f;
   for (int w = 0; w < nw; ++w) tot += red[w];
   const float* po = p.part_o + row * p.max_parts * p.D;
-  T* out = static_cast<T*>(p.out) + row * p.D;
   for (int d = tid; d < p.D; d += nthr) {
     float acc = 0.f;
     for (int i = 0; i < nparts; ++i) {
@@ -307,7 +333,7 @@ __device__ __forceinline__ void merge_row(const Params& p, long long row, int np
       }
       acc = fmaf(wt, __ldcg(po + (long long)i * p.D + d), acc);
     }
-    out[d] = from_float<T>(tot > 0.f ? acc / tot : 0.f);
+    store_out<T>(p, row, d, tot > 0.f ? acc / tot : 0.f);
   }
   sync();  // sm and red are reused by the next row
 }
@@ -349,7 +375,6 @@ __device__ __forceinline__ void merge_group(const Params& p, long long row0, int
     sinv[h] = den > 0.f ? 1.f / den : 0.f;
   }
   sync();
-  T* out = static_cast<T*>(p.out);
   for (int e = tid; e < GS * D; e += nthr) {
     const int h = e / D, d = e - h * D;
     const float* po = p.part_o + (row0 + h) * p.max_parts * D + d;
@@ -357,7 +382,7 @@ __device__ __forceinline__ void merge_group(const Params& p, long long row0, int
     float acc = 0.f;
 #pragma unroll 4
     for (int i = 0; i < np; ++i) acc = fmaf(w[i], __ldcg(po + (long long)i * D), acc);
-    out[(row0 + h) * D + d] = from_float<T>(acc * sinv[h]);
+    store_out<T>(p, row0 + h, d, acc * sinv[h]);
   }
 }
 

@@ -40,10 +40,9 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
   const ItemKind kind = decode_item(p, blockIdx.x, it);
   if (kind == kItemNone) return;
   const int D = p.D, GS = p.GS;
-  T* out = static_cast<T*>(p.out);
   if (kind == kItemZero) {
-    T* dst = out + ((long long)it.b * p.Hq + (long long)it.kvh * GS) * D;
-    for (int e = threadIdx.x; e < GS * D; e += blockDim.x) dst[e] = from_float<T>(0.f);
+    const long long row0 = (long long)it.b * p.Hq + (long long)it.kvh * GS;
+    for (int e = threadIdx.x; e < GS * D; e += blockDim.x) store_out<T>(p, row0 + e / D, e % D, 0.f);
     return;
   }
 
@@ -130,7 +129,7 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
       }
       const long long row = (long long)it.b * p.Hq + (long long)it.kvh * GS + hg0 + j;
       if (it.nparts == 1) {
-        out[row * D + d] = from_float<T>(den > 0.f ? num / den : 0.f);
+        store_out<T>(p, row, d, den > 0.f ? num / den : 0.f);
       } else {
         const long long pr = row * p.max_parts + it.part;
         p.part_o[pr * D + d] = num;
@@ -202,10 +201,10 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
   const ItemKind kind = decode_item(p, blockIdx.x, it);
   if (kind == kItemNone) return;
   const int GS = p.GS;
-  __half* out = static_cast<__half*>(p.out);
   if (kind == kItemZero) {
-    __half* dst = out + ((long long)it.b * p.Hq + (long long)it.kvh * GS) * D;
-    for (int e = threadIdx.x; e < GS * D; e += blockDim.x) dst[e] = __float2half_rn(0.f);
+    const long long row0 = (long long)it.b * p.Hq + (long long)it.kvh * GS;
+    for (int e = threadIdx.x; e < GS * D; e += blockDim.x)
+      store_out<__half>(p, row0 + e / D, e % D, 0.f);
     return;
   }
 
@@ -461,7 +460,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
       }
     }
     if (it.nparts == 1) {
-      out[(row0 + head) * D + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+      store_out<__half>(p, row0 + head, d, den > 0.f ? num / den : 0.f);
     } else {
       const long long pr = (row0 + head) * p.max_parts + it.part;
       p.part_o[pr * D + d] = num;
@@ -499,14 +498,56 @@ __global__ void __launch_bounds__(128) pa_reduce_kernel(const Params p, int cap)
   L = L < 0 ? 0 : ((long long)L > lim ? (int)lim : L);
   const int npages = (L + p.block_size - 1) / p.block_size;
   const int nparts = (npages + p.part_pages - 1) / p.part_pages;
+  pdl_launch_dependents();  // the gather barrier (if any) may be scheduled now
+  // Every CTA waits for the attention grid, also those with nothing to merge:
+  // this grid must not complete before the attention kernel has (later work
+  // on the stream is ordered after this grid, not after that kernel).
+  pdl_wait_primary();
   if (nparts <= 1) return;
-  pdl_wait_primary();  // the partials are the attention kernel's output
 #if XPA_REDUCE_GROUPED
   merge_group<T>(p, (long long)b * p.Hq + (long long)kvh * p.GS, nparts, threadIdx.x,
                  blockDim.x, sm_w, cap, CtaSync());
 #else
   merge_row<T>(p, row, nparts, threadIdx.x, blockDim.x, sm_w, cap, CtaSync());
 #endif
+}
+
+// ════════════════════════════════════════════════════════════════════════
+// Fused head gather: end-of-step barrier across the ranks' GPUs. Lane r
+// stores `step` into rank r's flag slot for this rank (release, system
+// scope), then waits until rank r's own signal for `step` has arrived in this
+// rank's flag array (acquire, system scope). Each wait is bounded; on expiry
+// the kernel raises NXT_PA_DEV_TIMEOUT and returns. One warp, one launch per
+// GPU; the ranks' barrier kernels run on different GPUs.
+// ════════════════════════════════════════════════════════════════════════
+struct PeerFlags {
+  unsigned long long* flags[kMaxPeers];  // rank r's flag array [world]
+};
+
+__global__ void __launch_bounds__(32) pa_peer_barrier_kernel(PeerFlags f, unsigned long long step,
+                                                             int rank, int world, int* status,
+                                                             unsigned long long budget_ns) {
+  const int r = threadIdx.x;
+  // Launched as a programmatic dependent: wait until the kernels that stored
+  // this rank's rows (attention, then merge) have completed; their writes,
+  // peer writes included, are flushed by then.
+  pdl_wait_primary();
+  if (r >= world) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f.flags[r] + rank), "l"(step)
+               : "memory");
+  const unsigned long long* mine = f.flags[rank] + r;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(mine) : "memory");
+    if (v >= step) break;
+    if (globaltimer_ns() - t0 >= budget_ns) {
+      if (status) atomicOr(status, kDevTimeout);
+      break;
+    }
+    __nanosleep(64);
+  }
 }
 
 // ════════════════════════════════════════════════════════════════════════
@@ -624,6 +665,23 @@ cudaError_t launch_reduce(const Params& p, int dtype_size, cudaStream_t st) {
   cfg.numAttrs = XPA_REDUCE_PDL ? 1 : 0;
   if (dtype_size == 4) return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<float>, p, cap);
   return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<__half>, p, cap);
+}
+
+cudaError_t launch_peer_barrier(void* const* flags, int world, int rank, unsigned long long step,
+                                int* status, unsigned long long budget_ns, cudaStream_t st) {
+  PeerFlags f{};
+  for (int r = 0; r < world && r < kMaxPeers; ++r)
+    f.flags[r] = static_cast<unsigned long long*>(flags[r]);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, pa_peer_barrier_kernel, f, step, rank, world, status, budget_ns);
 }
 
 }  // namespace xpa

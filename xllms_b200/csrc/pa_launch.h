@@ -21,4 +21,8 @@ cudaError_t launch_fast(const CUtensorMap& tk, const CUtensorMap& tv, const Para
 // Merges split-context partials; a no-op per row whose sequence has one partition.
 cudaError_t launch_reduce(const Params& p, int dtype_size, cudaStream_t st);
 
+// End-of-step barrier of the fused head gather (one warp; bounded waits).
+cudaError_t launch_peer_barrier(void* const* flags, int world, int rank, unsigned long long step,
+                                int* status, unsigned long long budget_ns, cudaStream_t st);
+
 }  // namespace xpa

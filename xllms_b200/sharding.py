@@ -13,6 +13,7 @@ torch.distributed carries the collective (NCCL on GPUs, gloo on CPU tests).
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Tuple
 
 
@@ -56,3 +57,131 @@ def interleave_heads(gathered, out=None):
         return view.reshape(B, P * h, D)
     out.view(B, P, h, D).copy_(view)
     return out
+
+
+# ── fused head gather over NVLink peer stores ────────────────────────────
+class NxtPaShard(ctypes.Structure):
+    """Layout of NxtPaShard (include/operator_api.h)."""
+    _fields_ = [
+        ("world_size", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("total_heads", ctypes.c_int),
+        ("head_offset", ctypes.c_int),
+        ("peer_out", ctypes.c_void_p * 8),
+        ("peer_flags", ctypes.c_void_p * 8),
+    ]
+
+
+class _DeviceArray:
+    """Zero-copy view of device memory for torch.as_tensor."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3,
+                                         "strides": None}
+
+
+def torch_exchange(group=None):
+    """Handle exchange over torch.distributed: bytes -> every rank's bytes."""
+    import torch.distributed as dist
+
+    def exchange(blob: bytes):
+        out = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, blob, group=group)
+        return [bytes(x) for x in out]
+    return exchange
+
+
+class FusedHeadGather:
+    """KV-head-sharded decode attention whose output all-gather is fused into
+    the kernels (nxt_paged_attention_sharded): each rank's kernels store its
+    heads straight into every rank's gather buffer over NVLink, and a bounded
+    cross-GPU barrier ends the step. The buffers are exchanged once, here,
+    through `exchange` (e.g. torch_exchange()).
+
+    run() enqueues step s and returns a [B, total_heads, D] view of half
+    (s & 1) of this rank's buffer, complete once the stream reaches it."""
+
+    def __init__(self, num_seqs: int, total_heads: int, head_size: int, dtype_size: int,
+                 world_size: int, rank: int, exchange, device=None):
+        from . import _native
+        self.lib = _native.xpa()
+        self.B, self.H, self.D, self.es = num_seqs, total_heads, head_size, dtype_size
+        self.world, self.rank = world_size, rank
+        if total_heads % world_size:
+            raise ValueError("total_heads must split evenly over the ranks")
+        half = num_seqs * total_heads * head_size * dtype_size
+        self.half_bytes = half
+        self.flags_off = (2 * half + 255) // 256 * 256
+        total = self.flags_off + 8 * world_size
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * _native.NXT_PA_IPC_HANDLE_BYTES)()
+        rc = self.lib.nxt_pa_peer_alloc(total, ctypes.byref(own), handle)
+        if rc != 0:
+            raise RuntimeError(f"nxt_pa_peer_alloc: {_native.strerror(rc)}")
+        self.own = own.value
+        handles = exchange(bytes(handle))
+        self.opened = []
+        self.shard = NxtPaShard()
+        self.shard.world_size, self.shard.rank = world_size, rank
+        self.shard.total_heads = total_heads
+        self.shard.head_offset = rank * (total_heads // world_size)
+        for r in range(world_size):
+            if r == rank:
+                base = self.own
+            else:
+                p = ctypes.c_void_p()
+                rc = self.lib.nxt_pa_peer_open(handles[r], ctypes.byref(p))
+                if rc != 0:
+                    raise RuntimeError(f"nxt_pa_peer_open(rank {r}): {_native.strerror(rc)}")
+                base = p.value
+                self.opened.append(base)
+            self.shard.peer_out[r] = base
+            self.shard.peer_flags[r] = base + self.flags_off
+        self.step = 0
+        self.device = device
+        # Views of the two halves, made once: importing device memory into
+        # torch per step would cost host time on every step.
+        import torch
+        typestr = "<f2" if self.es == 2 else "<f4"
+        self.views = [torch.as_tensor(_DeviceArray(self.own + i * self.half_bytes,
+                                                   (self.B, self.H, self.D), typestr),
+                                      device=device) for i in (0, 1)]
+
+    def output(self, step: int):
+        """[B, total_heads, D] view of the half that holds step `step`."""
+        return self.views[step & 1]
+
+    def run(self, query, key_cache, value_cache, block_tables, seq_lens, scale, num_blocks,
+            device_status=None, stream=None):
+        from . import _native
+        from .operator_api import _ptr, _stream_ptr
+        self.step += 1
+        B, Hq, D = query.shape
+        nb, Hkv, bs, _ = key_cache.shape
+        rc = self.lib.nxt_paged_attention_sharded(
+            ctypes.byref(self.shard), self.step, _ptr(query), _ptr(key_cache), _ptr(value_cache),
+            _ptr(block_tables), _ptr(seq_lens), B, Hq, D, Hkv, float(scale),
+            block_tables.shape[1], bs, self.es, Hkv * bs * D, bs * D, int(num_blocks),
+            _ptr(device_status), _stream_ptr(stream))
+        if rc != 0:
+            raise RuntimeError(f"nxt_paged_attention_sharded: {_native.strerror(rc)}")
+        return self.output(self.step)
+
+    def close(self, barrier=None):
+        """Unmaps the peers' buffers and frees this rank's; `barrier` (e.g.
+        torch.distributed.barrier) must keep every rank here until all are
+        done with every buffer."""
+        import torch
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        for p in self.opened:
+            self.lib.nxt_pa_peer_close(p)
+        self.opened = []
+        if barrier:
+            barrier()
+        self.views = []
+        if self.own:
+            self.lib.nxt_pa_peer_free(self.own)
+            self.own = 0
