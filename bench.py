@@ -103,70 +103,98 @@ _REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown"
 
 
 class ClockSampler:
-    """Samples SM clock and clock-event reasons of one GPU through NVML."""
+    """SM clock and clock-event reasons of the job's GPUs, sampled every 10 ms
+    by one external `nvidia-smi` process that rank 0 starts before warm-up (no
+    sampling work inside the ranks that enqueue GPU work). window() returns a
+    handle; summary(handle) keeps the samples whose timestamps fall inside
+    that window."""
 
-    def __init__(self, torch_device: int, period_s: float = 0.01):
-        self.period = period_s
-        self.samples = []
-        self.max_mhz = None
+    FIELDS = "timestamp,pci.bus_id,clocks.sm,clocks.max.sm,clocks_event_reasons.active"
+
+    def __init__(self, torch_devices, enabled: bool = True, period_ms: int = 10):
+        import subprocess
+        import tempfile
+        import torch
+        self.enabled = enabled
+        self.proc = None
         self.err = None
-        self._stop = threading.Event()
-        self._thr = None
-        try:
-            import pynvml
-            import torch
-            pynvml.nvmlInit()
-            p = torch.cuda.get_device_properties(torch_device)
-            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
-            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
-            self.nv = pynvml
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-        except Exception as exc:  # pragma: no cover - depends on the box
-            self.err = f"nvml unavailable: {exc}"
-            self.h = None
-
-    def _reasons(self):
-        nv = self.nv
-        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-            nv.nvmlDeviceGetCurrentClocksThrottleReasons
-        return int(fn(self.h))
-
-    def _run(self):
-        while not self._stop.is_set():
-            self.sample()
-            time.sleep(self.period)
-
-    def sample(self):
-        if self.h is None:
+        if not enabled:
             return
+        self.buses = set()
+        for d in torch_devices:
+            p = torch.cuda.get_device_properties(d)
+            self.buses.add(f"{p.pci_bus_id:02x}:{p.pci_device_id:02x}".lower())
+        self.tmp = tempfile.NamedTemporaryFile(prefix="clocks_", suffix=".csv", delete=False)
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+               f"-lms={period_ms}"]
+        # Query only the sampled GPUs: a query over every GPU of a large box
+        # takes longer than a short timed region.
         try:
-            mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
-            self.samples.append((mhz, self._reasons()))
-        except Exception as exc:  # pragma: no cover
-            self.err = str(exc)
+            out = subprocess.run(["nvidia-smi", "--query-gpu=index,pci.bus_id",
+                                  "--format=csv,noheader"], capture_output=True, text=True,
+                                 timeout=30).stdout
+            idx = [ln.split(",")[0].strip() for ln in out.splitlines()
+                   if any(b in ln.lower() for b in self.buses)]
+            if idx:
+                cmd.append("--id=" + ",".join(idx))
+        except Exception:
+            pass
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception as exc:  # pragma: no cover - depends on the box
+            self.err = f"nvidia-smi unavailable: {exc}"
 
-    def start(self):
-        if self.h is not None:
-            self.sample()
-            self._thr = threading.Thread(target=self._run, daemon=True)
-            self._thr.start()
+    @staticmethod
+    def now():
+        import datetime as _dt
+        return _dt.datetime.now()
 
-    def stop(self):
-        if self._thr is not None:
-            self._stop.set()
-            self._thr.join()
-        self.sample()
+    def close(self):
+        if self.proc is not None:
+            time.sleep(0.03)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.proc = None
 
-    def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
-                    "samples": 0, "note": self.err or "no samples"}
-        reasons = 0
-        for _, r in self.samples:
-            reasons |= r
+    def summary(self, t0, t1):
+        """Samples of the job's GPUs taken between host times t0 and t1."""
+        import datetime as _dt
+        if not self.enabled:
+            return None
+        mhz, maxes, reasons = [], [], 0
+        try:
+            with open(self.tmp.name) as f:
+                lines = f.readlines()
+        except OSError as exc:
+            lines, self.err = [], str(exc)
+        for line in lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 5:
+                continue
+            try:
+                ts = _dt.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+            except ValueError:
+                continue
+            if not (t0 <= ts <= t1):
+                continue
+            bus = parts[1].lower()
+            if not any(b in bus for b in self.buses):
+                continue
+            try:
+                mhz.append(float(parts[2]))
+                maxes.append(float(parts[3]))
+                reasons |= int(parts[4], 16)
+            except ValueError:
+                continue
+        if not mhz:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": self.err or "no sample fell inside the timed region"}
         names = sorted({n for bit, n in _REASONS.items() if reasons & bit})
-        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
-                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(maxes), "reasons": names,
+                "samples": len(mhz), "gpus": len(self.buses)}
 
 
 # ── CPU baseline: the reference's own CPU attention on the host cores ─────
@@ -289,6 +317,8 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
+    # rank 0 samples its own GPU; every rank runs the same work in lockstep
+    sampler = ClockSampler([local_rank], enabled=(rank == 0))
     for _ in range(args.warmup):
         step()
     barrier()
@@ -299,15 +329,14 @@ def run_ours(args, rank, world, local_rank):
     K = args.steps
     # Timed region 1: K plain steps -> value, ms_per_step, clocks.
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(local_rank)
     barrier()
-    clocks.start()
+    c0 = ClockSampler.now()
     start.record()
     for _ in range(K):
         step()
     stop.record()
     barrier()
-    clocks.stop()
+    c1 = ClockSampler.now()
     t_step = start.elapsed_time(stop) / K
     # output of the device-resident run
     resident = (fg.output(fg.step) if fused else (full if world > 1 else out)).clone()
@@ -334,8 +363,9 @@ def run_ours(args, rank, world, local_rank):
     if args.no_e2e:
         if fg is not None:
             fg.close(dist.barrier)
+        sampler.close()
         return _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, None,
-                       clocks, None, q, k, v, 0, 0, dev)
+                       sampler.summary(c0, c1), None, q, k, v, 0, 0, dev)
     plugin = PA.CudaBackendPlugin()
     # One pinned staging buffer holds the step's inputs (Q | block tables |
     # seq_lens), so each step issues a single host->device copy; the device
@@ -374,14 +404,15 @@ def run_ours(args, rank, world, local_rank):
         e2e_step()
     barrier()
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks_e2e = ClockSampler(local_rank)
-    clocks_e2e.start()
+    e0 = ClockSampler.now()
     e_start.record()
     for _ in range(K):
         e2e_step()
     e_stop.record()
     barrier()
-    clocks_e2e.stop()
+    e1 = ClockSampler.now()
+    sampler.close()
+    clocks, clocks_e2e = sampler.summary(c0, c1), sampler.summary(e0, e1)
     t_e2e = e_start.elapsed_time(e_stop) / K
     if not torch.equal(out_h.to(dev), resident):
         raise SystemExit("e2e output differs from the device-resident run")
@@ -484,9 +515,9 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
             "d2h_bytes_per_step": int(d2h),
             "api": "nxt_backend_run (libxllm_cuda_backend.so); per step one pinned H2D copy "
                    "(Q, block tables, seq_lens) and one D2H copy of the output",
-            "clocks": clocks_e2e.summary(),
+            "clocks": clocks_e2e,
         },
-        "clocks": clocks.summary(),
+        "clocks": clocks,
         "gpu_launches": launches_per_step * K * world,
         "gpu_launches_per_rank": launches_per_step * K,
     }

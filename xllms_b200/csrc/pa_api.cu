@@ -261,6 +261,16 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   p.part_pages = pl.part_pages;
   p.max_parts = pl.max_parts;
   p.scale_log2 = scale * 1.4426950408889634f;
+  {
+    auto a16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
+    bool ok = D % 8 == 0 && a16(part);
+    if (shard) {
+      for (int r = 0; r < shard->world_size; ++r) ok = ok && a16(shard->peer_out[r]);
+    } else {
+      ok = ok && a16(out);
+    }
+    p.vec8 = ok ? 1 : 0;
+  }
   if (shard) {
     p.npeers = shard->world_size;
     p.Hq_total = shard->total_heads;

@@ -41,6 +41,9 @@ struct Params {
   int npeers, Hq_total, head_offset;
   long long peer_off;
   void* peers[kMaxPeers];
+  // 1 when D % 8 == 0 and out / peer buffers and the partial workspace are
+  // 16-byte aligned: rows are then stored 8 elements (16 or 32 bytes) at a time.
+  int vec8;
 };
 
 // One unit of work: context partition `part` of (sequence b, KV head kvh).
@@ -283,6 +286,49 @@ __device__ __forceinline__ void store_out(const Params& p, long long row, int d,
     if (r < p.npeers) static_cast<T*>(p.peers[r])[off] = x;
 }
 
+// Stores elements d0 .. d0+7 of output row `row` with one 16-byte store (fp16)
+// or two (fp32) per destination. Requires Params::vec8.
+template <typename T>
+__device__ __forceinline__ void store_out8(const Params& p, long long row, int d0,
+                                           const float (&v)[8]) {
+  long long off;
+  if (p.npeers == 0) {
+    off = row * p.D + d0;
+  } else {
+    const long long b = row / p.Hq, h = row - b * p.Hq;
+    off = p.peer_off + (b * p.Hq_total + p.head_offset + h) * p.D + d0;
+  }
+  if constexpr (sizeof(T) == 2) {
+    uint4 u;
+    u.x = pack_half2(v[0], v[1]);
+    u.y = pack_half2(v[2], v[3]);
+    u.z = pack_half2(v[4], v[5]);
+    u.w = pack_half2(v[6], v[7]);
+    if (p.npeers == 0) {
+      *reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + off) = u;
+      return;
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+      if (r < p.npeers) *reinterpret_cast<uint4*>(static_cast<__half*>(p.peers[r]) + off) = u;
+  } else {
+    const float4 a = make_float4(v[0], v[1], v[2], v[3]), c = make_float4(v[4], v[5], v[6], v[7]);
+    if (p.npeers == 0) {
+      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
+      dst[0] = a;
+      dst[1] = c;
+      return;
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+      if (r < p.npeers) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.peers[r]) + off);
+        dst[0] = a;
+        dst[1] = c;
+      }
+  }
+}
+
 // ── split-context merge ─────────────────────────────────────────────────
 struct CtaSync {
   __device__ __forceinline__ void operator()() const { __syncthreads(); }
@@ -321,19 +367,47 @@ __device__ __forceinline__ void merge_row(const Params& p, long long row, int np
   float tot = 0.f;
   for (int w = 0; w < nw; ++w) tot += red[w];
   const float* po = p.part_o + row * p.max_parts * p.D;
-  for (int d = tid; d < p.D; d += nthr) {
-    float acc = 0.f;
-    for (int i = 0; i < nparts; ++i) {
-      float wt;
-      if (i < cap) {
-        wt = sm[i];
-      } else {
-        const float mp = __ldcg(ml + 2 * i);
-        wt = (M == -INFINITY || mp == -INFINITY) ? 0.f : ex2(mp - M);
+  if (p.vec8) {
+    for (int c = tid; c < p.D / 8; c += nthr) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int i = 0; i < nparts; ++i) {
+        float wt;
+        if (i < cap) {
+          wt = sm[i];
+        } else {
+          const float mp = __ldcg(ml + 2 * i);
+          wt = (M == -INFINITY || mp == -INFINITY) ? 0.f : ex2(mp - M);
+        }
+        const float4* src = reinterpret_cast<const float4*>(po + (long long)i * p.D + c * 8);
+        const float4 a = __ldcg(src), b = __ldcg(src + 1);
+        acc[0] = fmaf(wt, a.x, acc[0]);
+        acc[1] = fmaf(wt, a.y, acc[1]);
+        acc[2] = fmaf(wt, a.z, acc[2]);
+        acc[3] = fmaf(wt, a.w, acc[3]);
+        acc[4] = fmaf(wt, b.x, acc[4]);
+        acc[5] = fmaf(wt, b.y, acc[5]);
+        acc[6] = fmaf(wt, b.z, acc[6]);
+        acc[7] = fmaf(wt, b.w, acc[7]);
       }
-      acc = fmaf(wt, __ldcg(po + (long long)i * p.D + d), acc);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = tot > 0.f ? acc[k] / tot : 0.f;
+      store_out8<T>(p, row, c * 8, acc);
     }
-    store_out<T>(p, row, d, tot > 0.f ? acc / tot : 0.f);
+  } else {
+    for (int d = tid; d < p.D; d += nthr) {
+      float acc = 0.f;
+      for (int i = 0; i < nparts; ++i) {
+        float wt;
+        if (i < cap) {
+          wt = sm[i];
+        } else {
+          const float mp = __ldcg(ml + 2 * i);
+          wt = (M == -INFINITY || mp == -INFINITY) ? 0.f : ex2(mp - M);
+        }
+        acc = fmaf(wt, __ldcg(po + (long long)i * p.D + d), acc);
+      }
+      store_out<T>(p, row, d, tot > 0.f ? acc / tot : 0.f);
+    }
   }
   sync();  // sm and red are reused by the next row
 }

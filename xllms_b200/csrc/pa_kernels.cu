@@ -444,27 +444,49 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
   }
   named_bar_sync(1, NWC * 32);
 
+  // Each thread merges 8 consecutive d of one head (RS keeps rows 16-byte
+  // aligned, so the shared-memory reads are two float4 loads per warp state).
   const long long row0 = (long long)it.b * p.Hq + (long long)it.kvh * GS;
-  for (int e = threadIdx.x; e < GS * D; e += NWC * 32) {
-    const int head = e / D, d = e - head * D;
+  constexpr int CH = D / 8;
+  for (int e = threadIdx.x; e < GS * CH; e += NWC * 32) {
+    const int head = e / CH, d0 = (e - head * CH) * 8;
     float M = -INFINITY;
 #pragma unroll
     for (int ww = 0; ww < NWC; ++ww) M = fmaxf(M, sm_ml[(ww * GS + head) * 2]);
-    float num = 0.f, den = 0.f;
+    float num[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float den = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
       for (int ww = 0; ww < NWC; ++ww) {
         const float wt = ex2(sm_ml[(ww * GS + head) * 2] - M);
         den = fmaf(wt, sm_ml[(ww * GS + head) * 2 + 1], den);
-        num = fmaf(wt, sm_o[(ww * GS + head) * RS + d], num);
+        const float4* src = reinterpret_cast<const float4*>(sm_o + (ww * GS + head) * RS + d0);
+        const float4 a = src[0], b = src[1];
+        num[0] = fmaf(wt, a.x, num[0]);
+        num[1] = fmaf(wt, a.y, num[1]);
+        num[2] = fmaf(wt, a.z, num[2]);
+        num[3] = fmaf(wt, a.w, num[3]);
+        num[4] = fmaf(wt, b.x, num[4]);
+        num[5] = fmaf(wt, b.y, num[5]);
+        num[6] = fmaf(wt, b.z, num[6]);
+        num[7] = fmaf(wt, b.w, num[7]);
       }
     }
     if (it.nparts == 1) {
-      store_out<__half>(p, row0 + head, d, den > 0.f ? num / den : 0.f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) num[k] = den > 0.f ? num[k] / den : 0.f;
+      if (p.vec8) {
+        store_out8<__half>(p, row0 + head, d0, num);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) store_out<__half>(p, row0 + head, d0 + k, num[k]);
+      }
     } else {
       const long long pr = (row0 + head) * p.max_parts + it.part;
-      p.part_o[pr * D + d] = num;
-      if (d == 0) {
+      float* dst = p.part_o + pr * D + d0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) dst[k] = num[k];
+      if (d0 == 0) {
         p.part_ml[2 * pr] = M;
         p.part_ml[2 * pr + 1] = den;
       }
