@@ -203,6 +203,41 @@ int nxt_paged_attention_noalloc(
  * tiny budget makes the waits run out on purpose without faulting the GPU. */
 uint64_t nxt_paged_attention_set_wait_budget_ns(uint64_t budget_ns);
 
+/* ── extension: KV append (no paged writer exists in the
+ * reference, whose decode loop memcpy's each token into a contiguous cache,
+ * examples/text_gen.c:1274-1278) ──────────────────────────────────────
+ * Writes token t's key and value rows (key/value[t*token_stride + h*head_size
+ * + d], h < num_kv_heads) into the paged pools at page slot_mapping[t] /
+ * block_size, slot slot_mapping[t] % block_size; a negative slot skips the
+ * token. Bit-exact copy. */
+int nxt_reshape_and_cache(
+    const void *key, const void *value,
+    void *key_cache, void *value_cache,
+    const int64_t *slot_mapping, int num_tokens,
+    int num_kv_heads, int head_size, int block_size, int dtype_size,
+    int64_t kv_block_stride, int64_t kv_head_stride, int64_t token_stride,
+    nxt_stream_t stream);
+
+/* Decode step with the append fused in: writes new_key/new_value
+ * ([num_seqs][num_kv_heads][head_size], one new token per sequence) at
+ * slot_mapping[b], then runs nxt_paged_attention_ex over seq_lens (which
+ * already count the new token). The attention grid is launched as a
+ * programmatic dependent of the append: only the load of each sequence's
+ * last page waits for the append, every other page streams meanwhile. */
+int nxt_paged_attention_append_ex(
+    void *out, const void *query,
+    void *key_cache, void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    const void *new_key, const void *new_value, const int64_t *slot_mapping,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq,
+    int block_size, int dtype_size,
+    int64_t kv_block_stride, int64_t kv_head_stride,
+    int64_t num_blocks,
+    int *device_status,
+    nxt_stream_t stream);
+
 /* ── extension: KV-head sharding with the output all-gather fused in ────
  * For P GPUs of one box, one process or thread per GPU. Rank r owns KV
  * heads [r*Hkv/P, (r+1)*Hkv/P) with their query heads (head_offset =

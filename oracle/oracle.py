@@ -47,6 +47,9 @@ def oracle_lib() -> ctypes.CDLL:
         lib.pa_oracle_merge_partials.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I]
         lib.pa_oracle_gather_checksum.restype = _I
         lib.pa_oracle_gather_checksum.argtypes = [_P, _P, _P, _I, _I, _I, _I, _I, _I64]
+        lib.pa_oracle_reshape_and_cache.restype = None
+        lib.pa_oracle_reshape_and_cache.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I,
+                                                    _I64, _I64, _I64]
         lib.pa_gather_mix.restype = ctypes.c_uint64
         lib.pa_gather_mix.argtypes = [ctypes.c_uint64] * 3
         lib.pa_half_to_float.restype = _F
@@ -138,6 +141,18 @@ def merge_partials(m, l, o, seq_lens, block_size, part_pages) -> np.ndarray:
         _c(out), _c(_as(m, np.float32)), _c(_as(l, np.float32)), _c(_as(o, np.float32)),
         _c(_as(seq_lens, np.int32)), B, H, D, block_size, part_pages, P)
     return out
+
+
+def reshape_and_cache(key, value, key_cache, value_cache, slots, block_size=16):
+    """In-place scatter of key/value [T][Hkv][D] into the pools [NB][Hkv][P][D]."""
+    key = np.ascontiguousarray(key)
+    value = np.ascontiguousarray(value)
+    slots = _as(slots, np.int64)
+    T, Hkv, D = key.shape
+    assert key_cache.flags.c_contiguous and value_cache.flags.c_contiguous
+    oracle_lib().pa_oracle_reshape_and_cache(
+        _c(key), _c(value), _c(key_cache), _c(value_cache), _c(slots), T, Hkv, D, block_size,
+        key.dtype.itemsize, Hkv * block_size * D, block_size * D, Hkv * D)
 
 
 def gather_checksum(block_tables, seq_lens, num_heads, num_kv_heads, block_size=16,

@@ -391,3 +391,22 @@ int pa_oracle_gather_checksum(uint64_t *out, const int *block_tables,
     }
     return 0;
 }
+
+void pa_oracle_reshape_and_cache(const void *key, const void *value, void *key_cache,
+                                 void *value_cache, const int64_t *slots, int num_tokens,
+                                 int num_kv_heads, int head_size, int block_size,
+                                 int elem_size, int64_t kv_block_stride,
+                                 int64_t kv_head_stride, int64_t token_stride) {
+    const size_t row = (size_t)head_size * (size_t)elem_size;
+    for (int t = 0; t < num_tokens; t++) {
+        const int64_t slot = slots[t];
+        if (slot < 0) continue;
+        const int64_t page = slot / block_size, s = slot % block_size;
+        for (int h = 0; h < num_kv_heads; h++) {
+            const int64_t dst = page * kv_block_stride + (int64_t)h * kv_head_stride + s * head_size;
+            const int64_t src = (int64_t)t * token_stride + (int64_t)h * head_size;
+            memcpy((char *)key_cache + dst * elem_size, (const char *)key + src * elem_size, row);
+            memcpy((char *)value_cache + dst * elem_size, (const char *)value + src * elem_size, row);
+        }
+    }
+}

@@ -89,6 +89,17 @@ void pa_oracle_merge_partials(float *out, const float *m, const float *l,
                               int num_seqs, int num_heads, int head_size,
                               int block_size, int part_pages, int max_parts);
 
+/* KV append restated: token t's rows (t*token_stride + h*head_size + d) are
+ * copied to page slots[t]/block_size, slot slots[t]%block_size of the pools
+ * (negative slot: skipped). elem_size bytes per element (bit copy). The
+ * reference has no paged writer; its decode loop copies each new token into
+ * a contiguous cache (examples/text_gen.c:1274-1278). */
+void pa_oracle_reshape_and_cache(const void *key, const void *value, void *key_cache,
+                                 void *value_cache, const int64_t *slots, int num_tokens,
+                                 int num_kv_heads, int head_size, int block_size,
+                                 int elem_size, int64_t kv_block_stride,
+                                 int64_t kv_head_stride, int64_t token_stride);
+
 /* Index-logic checksum: for every (seq, q head), the wrapping 64-bit sum of
  * pa_gather_mix(phys, slot, kv_head) over every token the attention reads. */
 uint64_t pa_gather_mix(uint64_t phys, uint64_t slot, uint64_t kv_head);

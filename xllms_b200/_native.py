@@ -57,6 +57,13 @@ SIGNATURES = {
          _VP, _VP],
     ),
     "nxt_paged_attention_profile_next": (_I, [_VP, _VP]),
+    "nxt_reshape_and_cache": (
+        _I, [_CVP, _CVP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I64, _I64, _I64, _VP]),
+    "nxt_paged_attention_append_ex": (
+        _I,
+        [_VP, _CVP, _VP, _VP, _IP, _IP, _CVP, _CVP, _VP, _I, _I, _I, _I, _F, _I, _I, _I, _I64,
+         _I64, _I64, _VP, _VP],
+    ),
     "nxt_pa_peer_alloc": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p), _VP]),
     "nxt_pa_peer_open": (_I, [_VP, ctypes.POINTER(ctypes.c_void_p)]),
     "nxt_pa_peer_close": (_I, [_VP]),

@@ -191,7 +191,7 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
         int B, int Hq, int D, int Hkv, float scale, int max_blocks, int bs, int ds,
         long long kbs, long long khs, long long num_blocks, void* ws, size_t ws_bytes,
         int* dev_status, cudaStream_t st, const NxtPaShard* shard = nullptr,
-        uint64_t step = 0) {
+        uint64_t step = 0, bool after_append = false) {
   if (shard) {
     if (shard->world_size < 1 || shard->world_size > NXT_PA_MAX_PEERS || shard->rank < 0 ||
         shard->rank >= shard->world_size || step == 0 || shard->head_offset < 0 ||
@@ -261,6 +261,7 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   p.part_pages = pl.part_pages;
   p.max_parts = pl.max_parts;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.after_append = after_append ? 1 : 0;
   {
     auto a16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
     bool ok = D % 8 == 0 && a16(part);
@@ -444,6 +445,62 @@ int nxt_paged_attention_release_workspaces(void) {
   }
   if (have_prev) cudaSetDevice(prev);
   return rc;
+}
+
+int nxt_reshape_and_cache(const void* key, const void* value, void* key_cache, void* value_cache,
+                          const int64_t* slot_mapping, int num_tokens, int num_kv_heads,
+                          int head_size, int block_size, int dtype_size, int64_t kv_block_stride,
+                          int64_t kv_head_stride, int64_t token_stride, nxt_stream_t stream) {
+  if (num_tokens < 0) return NXT_PA_EINVAL;
+  if (num_tokens == 0) return NXT_PA_OK;
+  if (!key || !value || !key_cache || !value_cache || !slot_mapping) return NXT_PA_EINVAL;
+  if (num_kv_heads <= 0 || head_size <= 0 || head_size > 256 || block_size <= 0 ||
+      (dtype_size != 2 && dtype_size != 4) || kv_block_stride < 0 || kv_head_stride < 0 ||
+      token_stride < (int64_t)num_kv_heads * head_size)
+    return NXT_PA_EINVAL;
+  xpa::AppendParams a{};
+  a.key = key;
+  a.value = value;
+  a.key_cache = key_cache;
+  a.value_cache = value_cache;
+  a.slots = reinterpret_cast<const long long*>(slot_mapping);
+  a.kv_block_stride = kv_block_stride;
+  a.kv_head_stride = kv_head_stride;
+  a.token_stride = token_stride;
+  a.num_tokens = num_tokens;
+  a.Hkv = num_kv_heads;
+  a.D = head_size;
+  a.block_size = block_size;
+  auto a16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
+  const int64_t es = dtype_size;
+  a.vec16 = ((head_size * es) % 16 == 0 && (kv_block_stride * es) % 16 == 0 &&
+             (kv_head_stride * es) % 16 == 0 && (token_stride * es) % 16 == 0 && a16(key) &&
+             a16(value) && a16(key_cache) && a16(value_cache))
+                ? 1
+                : 0;
+  return map_cuda(xpa::launch_append(a, dtype_size, static_cast<cudaStream_t>(stream)));
+}
+
+int nxt_paged_attention_append_ex(void* out, const void* query, void* key_cache,
+                                  void* value_cache, const int* block_tables, const int* seq_lens,
+                                  const void* new_key, const void* new_value,
+                                  const int64_t* slot_mapping, int num_seqs, int num_heads,
+                                  int head_size, int num_kv_heads, float scale,
+                                  int max_num_blocks_per_seq, int block_size, int dtype_size,
+                                  int64_t kv_block_stride, int64_t kv_head_stride,
+                                  int64_t num_blocks, int* device_status, nxt_stream_t stream) {
+  int rc = check_args(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs,
+                      num_heads, head_size, num_kv_heads, max_num_blocks_per_seq, block_size,
+                      dtype_size, kv_block_stride, kv_head_stride);
+  if (rc != NXT_PA_OK || num_seqs == 0) return rc;
+  rc = nxt_reshape_and_cache(new_key, new_value, key_cache, value_cache, slot_mapping, num_seqs,
+                             num_kv_heads, head_size, block_size, dtype_size, kv_block_stride,
+                             kv_head_stride, (int64_t)num_kv_heads * head_size, stream);
+  if (rc != NXT_PA_OK) return rc;
+  return run(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads,
+             head_size, num_kv_heads, scale, max_num_blocks_per_seq, block_size, dtype_size,
+             kv_block_stride, kv_head_stride, num_blocks, nullptr, 0, device_status,
+             static_cast<cudaStream_t>(stream), nullptr, 0, true);
 }
 
 int nxt_pa_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle) {

@@ -44,6 +44,23 @@ struct Params {
   // 1 when D % 8 == 0 and out / peer buffers and the partial workspace are
   // 16-byte aligned: rows are then stored 8 elements (16 or 32 bytes) at a time.
   int vec8;
+  // 1 when this grid was launched as a programmatic dependent of the KV
+  // append kernel: a sequence's last page may only be read after
+  // griddepcontrol.wait (the appended token lives there).
+  int after_append;
+};
+
+// KV append: token t's rows key/value[t*token_stride + h*D + d] go to the
+// pool slot slots[t] (page slot/block_size, slot slot%block_size).
+struct AppendParams {
+  const void* key;
+  const void* value;
+  void* key_cache;
+  void* value_cache;
+  const long long* slots;
+  long long kv_block_stride, kv_head_stride, token_stride;
+  int num_tokens, Hkv, D, block_size;
+  int vec16;  // every row 16-byte aligned: copy 16 bytes per lane
 };
 
 // One unit of work: context partition `part` of (sequence b, KV head kvh).

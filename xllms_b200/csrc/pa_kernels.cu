@@ -16,6 +16,8 @@
 // phys*kv_block_stride + kvh*kv_head_stride + slot*D + d
 // (operators/page_attention_v2.cu:143-146), zero row for seq_len 0
 // (operators/page_attention.cu:157).
+#include <utility>
+
 #include "pa_device.cuh"
 #include "pa_launch.h"
 
@@ -47,6 +49,7 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
   }
 
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (p.after_append) pdl_wait_primary();  // appended tokens are read like any other
   const T* Q = static_cast<const T*>(p.q);
   const T* K = static_cast<const T*>(p.k);
   const T* V = static_cast<const T*>(p.v);
@@ -234,6 +237,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
     const int* bt_row = p.block_tables + (long long)it.b * p.max_blocks;
     int ent = -1;
     int ok = 1, issued = 0;
+    const int last_page = (it.L + 15) / 16 - 1;  // holds an appended token
     for (int j = 0; j < np; ++j) {
       if ((j & 31) == 0) {
         const int idx = it.page_begin + j + lane;
@@ -242,6 +246,8 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
       const int phys = __shfl_sync(0xffffffffu, ent, j & 31);
       if (lane == 0) {
         const int s = j % STAGES;
+        // Only the page an append kernel wrote into must wait for that kernel.
+        if (p.after_append && it.page_begin + j == last_page) pdl_wait_primary();
         if (j >= STAGES && !mbar_wait(bar_empty + 8 * s, ((j / STAGES) + 1) & 1, budget)) {
           raise_status(p, kDevTimeout);
           ok = 0;
@@ -573,15 +579,71 @@ __global__ void __launch_bounds__(32) pa_peer_barrier_kernel(PeerFlags f, unsign
 }
 
 // ════════════════════════════════════════════════════════════════════════
+// KV append ("reshape and cache"): token t's K and V rows ([Hkv][D] each)
+// go to page slot_mapping[t] / block_size, slot slot_mapping[t] % block_size
+// of the paged pools; a negative slot skips the token. One warp per
+// (token, KV head), 16-byte copies when every row is 16-byte aligned. It
+// triggers its dependents at start, so an attention grid launched after it
+// as a programmatic dependent starts streaming at once.
+// ════════════════════════════════════════════════════════════════════════
+template <typename T>
+__global__ void __launch_bounds__(128) pa_append_kernel(AppendParams a) {
+  pdl_launch_dependents();
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long long)a.num_tokens * a.Hkv) return;
+  const int t = (int)(w / a.Hkv), h = (int)(w % a.Hkv);
+  const long long slot = a.slots[t];
+  if (slot < 0) return;
+  const long long page = slot / a.block_size, s = slot % a.block_size;
+  const long long dst = page * a.kv_block_stride + (long long)h * a.kv_head_stride + s * a.D;
+  const long long src = (long long)t * a.token_stride + (long long)h * a.D;
+  const T* k = static_cast<const T*>(a.key) + src;
+  const T* v = static_cast<const T*>(a.value) + src;
+  T* kc = static_cast<T*>(a.key_cache) + dst;
+  T* vc = static_cast<T*>(a.value_cache) + dst;
+  if (a.vec16) {
+    constexpr int E = 16 / sizeof(T);
+    for (int i = lane; i < a.D / E; i += 32) {
+      reinterpret_cast<uint4*>(kc)[i] = __ldg(reinterpret_cast<const uint4*>(k) + i);
+      reinterpret_cast<uint4*>(vc)[i] = __ldg(reinterpret_cast<const uint4*>(v) + i);
+    }
+  } else {
+    for (int i = lane; i < a.D; i += 32) {
+      kc[i] = k[i];
+      vc[i] = v[i];
+    }
+  }
+}
+
+// ════════════════════════════════════════════════════════════════════════
 // Launchers
 // ════════════════════════════════════════════════════════════════════════
 namespace {
 
+// Launches `kern` on `st`; as a programmatic dependent of the previous
+// launch on the stream when `pdl` is set.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                      cudaStream_t st, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <typename T, int DPL, int HG>
 cudaError_t launch_generic_t(const Params& p, cudaStream_t st) {
   const long long grid = (long long)p.B * p.Hkv * p.max_parts;
-  pa_generic_kernel<T, DPL, HG><<<(unsigned)grid, 128, 0, st>>>(p);
-  return cudaGetLastError();
+  return launch_ex(pa_generic_kernel<T, DPL, HG>, (unsigned)grid, 128, 0, st,
+                   p.after_append != 0, p);
 }
 
 template <typename T, int DPL>
@@ -634,8 +696,8 @@ cudaError_t launch_fast_t(const CUtensorMap& tk, const CUtensorMap& tv, const Pa
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   if (e != cudaSuccess) return e;
   const long long grid = (long long)p.B * p.Hkv * p.max_parts;
-  kern<<<(unsigned)grid, C::kThreads, C::kSmem, st>>>(tk, tv, p);
-  return cudaGetLastError();
+  return launch_ex(kern, (unsigned)grid, C::kThreads, C::kSmem, st, p.after_append != 0, tk, tv,
+                   p);
 }
 
 }  // namespace
@@ -687,6 +749,17 @@ cudaError_t launch_reduce(const Params& p, int dtype_size, cudaStream_t st) {
   cfg.numAttrs = XPA_REDUCE_PDL ? 1 : 0;
   if (dtype_size == 4) return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<float>, p, cap);
   return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<__half>, p, cap);
+}
+
+cudaError_t launch_append(const AppendParams& a, int dtype_size, cudaStream_t st) {
+  const long long warps = (long long)a.num_tokens * a.Hkv;
+  const unsigned grid = (unsigned)((warps * 32 + 127) / 128);
+  if (grid == 0) return cudaSuccess;
+  if (dtype_size == 4)
+    pa_append_kernel<float><<<grid, 128, 0, st>>>(a);
+  else
+    pa_append_kernel<__half><<<grid, 128, 0, st>>>(a);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_peer_barrier(void* const* flags, int world, int rank, unsigned long long step,

@@ -21,6 +21,9 @@ cudaError_t launch_fast(const CUtensorMap& tk, const CUtensorMap& tv, const Para
 // Merges split-context partials; a no-op per row whose sequence has one partition.
 cudaError_t launch_reduce(const Params& p, int dtype_size, cudaStream_t st);
 
+// KV append ("reshape and cache") of new tokens into the paged pools.
+cudaError_t launch_append(const AppendParams& a, int dtype_size, cudaStream_t st);
+
 // End-of-step barrier of the fused head gather (one warp; bounded waits).
 cudaError_t launch_peer_barrier(void* const* flags, int world, int rank, unsigned long long step,
                                 int* status, unsigned long long budget_ns, cudaStream_t st);

@@ -253,3 +253,50 @@ def make_input(query, key_cache, value_cache, block_tables, seq_lens, scale=None
     pa.kv_head_stride = bs * D
     pa.stream = _stream_ptr(stream)
     return pa
+
+
+# ── KV append ─────────────────────────────────────────────────────────────
+def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, stream=None) -> None:
+    """Scatter key/value [T, Hkv, D] into the pools [NB, Hkv, P, D] at
+    slot_mapping[t] (int64; page = slot // P, slot % P; negative: skipped)."""
+    T, Hkv, D = key.shape
+    nb, hk, bs, dk = key_cache.shape
+    if (hk != Hkv or dk != D or tuple(value.shape) != tuple(key.shape)
+            or tuple(value_cache.shape) != tuple(key_cache.shape)
+            or not (key_cache.is_contiguous() and value_cache.is_contiguous())
+            or key.stride(1) != D or value.stride() != key.stride()
+            or slot_mapping.numel() < T):
+        raise PagedAttentionError(_native.NXT_PA_EINVAL, "reshape_and_cache: shapes")
+    rc = _native.xpa().nxt_reshape_and_cache(
+        _ptr(key), _ptr(value), _ptr(key_cache), _ptr(value_cache), _ptr(slot_mapping), T, Hkv, D,
+        bs, _dtype_size(key), Hkv * bs * D, bs * D, key.stride(0), _stream_ptr(stream))
+    if rc != _native.NXT_PA_OK:
+        raise PagedAttentionError(rc, "nxt_reshape_and_cache")
+
+
+def paged_attention_append(query, key_cache, value_cache, block_tables, seq_lens, new_key,
+                           new_value, slot_mapping, *, scale=None, out=None, num_blocks=None,
+                           device_status=None, stream=None):
+    """One decode step with the KV append fused in: new_key/new_value
+    [B, Hkv, D] are written at slot_mapping[b] and included in the attention
+    (seq_lens count them)."""
+    import torch
+    B, Hq, D = query.shape
+    nb, Hkv, bs, _ = key_cache.shape
+    if (tuple(value_cache.shape) != tuple(key_cache.shape)
+            or tuple(new_key.shape) != (B, Hkv, D) or tuple(new_value.shape) != (B, Hkv, D)
+            or not (new_key.is_contiguous() and new_value.is_contiguous())
+            or slot_mapping.numel() < B):
+        raise PagedAttentionError(_native.NXT_PA_EINVAL, "paged_attention_append: shapes")
+    if out is None:
+        out = torch.empty_like(query)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    rc = _native.xpa().nxt_paged_attention_append_ex(
+        _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+        _ptr(seq_lens), _ptr(new_key), _ptr(new_value), _ptr(slot_mapping), B, Hq, D, Hkv,
+        float(scale), block_tables.shape[1], bs, _dtype_size(query), Hkv * bs * D, bs * D,
+        nb if num_blocks is None else int(num_blocks), _ptr(device_status), _stream_ptr(stream))
+    if rc != _native.NXT_PA_OK:
+        raise PagedAttentionError(rc, "nxt_paged_attention_append_ex")
+    return out
