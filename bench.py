@@ -54,6 +54,9 @@ def parse_args():
                     help="N > 1: fused = kernels store each rank's heads into every GPU's "
                          "buffer over NVLink (nxt_paged_attention_sharded); nccl = NCCL "
                          "all-gather + head interleave")
+    ap.add_argument("--prefix", choices=["on", "off"], default="on",
+                    help="c4: on = shared-prefix (cascade) attention over the radix prefix "
+                         "groups (nxt_paged_attention_prefix_ex); off = plain decode kernels")
     ap.add_argument("--seqs", type=int, default=0,
                     help="sequences per GPU for c2/c4/c5 (default: the BASELINE size); smaller "
                          "values make the small cases the ncu captures run on")
@@ -300,12 +303,21 @@ def run_ours(args, rank, world, local_rank):
     split = PA.workspace_size(batch.num_seqs, batch.num_heads, batch.head_size,
                               batch.num_kv_heads, batch.max_blocks, batch.block_size,
                               batch.dtype_size) > 0
-    # attention kernel (+ split-context merge) (+ the fused gather's barrier)
-    launches_per_step = 1 + (1 if split else 0) + (1 if fused else 0)
+    cascade = (args.prefix == "on" and bool(batch.prefix_groups) and world == 1
+               and path == _native.NXT_PA_PATH_TMA_MMA)
+    groups = PA.PrefixGroups(batch.prefix_groups, batch.num_seqs, dev) if cascade else None
+    # attention kernel (+ split-context merge) (+ the fused gather's barrier);
+    # cascade: prefix kernel + suffix kernel + merge
+    launches_per_step = (3 if cascade else
+                         1 + (1 if split else 0) + (1 if fused else 0))
 
     def step():
         if fused:
             fg.run(q, k, v, bt, sl, batch.scale, batch.num_blocks)
+            return
+        if cascade:
+            PA.paged_attention_prefix(q, k, v, bt, sl, groups, out=out,
+                                      num_blocks=batch.num_blocks)
             return
         PA.paged_attention(q, k, v, bt, sl, out=out, num_blocks=batch.num_blocks)
         if world > 1:
@@ -365,20 +377,30 @@ def run_ours(args, rank, world, local_rank):
             fg.close(dist.barrier)
         sampler.close()
         return _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, None,
-                       sampler.summary(c0, c1), None, q, k, v, 0, 0, dev)
+                       sampler.summary(c0, c1), None, q, k, v, 0, 0, dev, cascade)
     plugin = PA.CudaBackendPlugin()
     # One pinned staging buffer holds the step's inputs (Q | block tables |
     # seq_lens), so each step issues a single host->device copy; the device
     # side is one buffer viewed as the three tensors.
-    nq, nbt, nsl = q.numel() * q.element_size(), bt.numel() * 4, sl.numel() * 4
-    stage_h = torch.empty(nq + nbt + nsl, dtype=torch.uint8).pin_memory()
-    stage_h[:nq].copy_(q.cpu().view(-1).view(torch.uint8))
-    stage_h[nq:nq + nbt].copy_(bt.cpu().view(-1).view(torch.uint8))
-    stage_h[nq + nbt:].copy_(sl.cpu().view(-1).view(torch.uint8))
+    # A cascade step's prefix groups (prefix pages per sequence, group
+    # offsets, members) ride in the same copy.
+    host_parts = [q.cpu(), bt.cpu(), sl.cpu()]
+    if cascade:
+        host_parts += [torch.from_numpy(a) for a in
+                       PA.PrefixGroups.host_arrays(batch.prefix_groups, batch.num_seqs)]
+    sizes = [t.numel() * t.element_size() for t in host_parts]
+    stage_h = torch.empty(sum(sizes), dtype=torch.uint8).pin_memory()
     stage_d = torch.empty_like(stage_h, device=dev)
-    q_d = stage_d[:nq].view(q.dtype).view(q.shape)
-    bt_d = stage_d[nq:nq + nbt].view(torch.int32).view(bt.shape)
-    sl_d = stage_d[nq + nbt:].view(torch.int32).view(sl.shape)
+    views, o = [], 0
+    for t, n in zip(host_parts, sizes):
+        stage_h[o:o + n].copy_(t.reshape(-1).view(torch.uint8))
+        views.append(stage_d[o:o + n].view(t.dtype).view(t.shape))
+        o += n
+    q_d, bt_d, sl_d = views[:3]
+    groups_d = None
+    if cascade:
+        groups_d = PA.PrefixGroups(batch.prefix_groups, batch.num_seqs, prefix_pages=views[3],
+                                   offsets=views[4], members=views[5])
     out_d = torch.empty_like(out)
     res = full if (world > 1 and not fused) else out_d
     out_h = torch.empty((batch.num_seqs, batch.total_heads, batch.head_size),
@@ -393,7 +415,11 @@ def run_ours(args, rank, world, local_rank):
             out_h.copy_(fg.run(q_d, k, v, bt_d, sl_d, batch.scale, batch.num_blocks),
                         non_blocking=True)
             return
-        if plugin.run(pa_in, out_d) != 0:
+        if cascade:
+            # the C-ABI cascade entry point (the plugin descriptor has no group fields)
+            PA.paged_attention_prefix(q_d, k, v, bt_d, sl_d, groups_d, out=out_d,
+                                      num_blocks=batch.num_blocks)
+        elif plugin.run(pa_in, out_d) != 0:
             raise SystemExit("nxt_backend_run failed")
         if world > 1:
             sharding.gather_heads(out_d, gathered)
@@ -422,11 +448,11 @@ def run_ours(args, rank, world, local_rank):
     h2d = stage_h.numel()
     d2h = out_h.numel() * out_h.element_size()
     return _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t_e2e,
-                   clocks, clocks_e2e, q, k, v, h2d, d2h, dev)
+                   clocks, clocks_e2e, q, k, v, h2d, d2h, dev, cascade)
 
 
 def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t_e2e, clocks,
-            clocks_e2e, q, k, v, h2d, d2h, dev):
+            clocks_e2e, q, k, v, h2d, d2h, dev, cascade=False):
     import torch
     import torch.distributed as dist
     K = args.steps
@@ -487,7 +513,8 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
                             f"KV-head sharding x{world} + NCCL all-gather of outputs"),
             "l2": f"no flush: each step reads {tot_kv / world / 1e9:.2f} GB of KV per GPU "
                   f"(> {L2_BYTES >> 20} MB L2)",
-            "path": {1: "tma_mma", 2: "generic"}.get(path, "none"),
+            "path": {1: "tma_mma", 2: "generic"}.get(path, "none") +
+                    (" + shared-prefix (cascade) kernel" if cascade else ""),
         },
         "pct_hbm_peak": round(100.0 * (tot_ub / world) / (t_step * 1e-3) / 1e9 / peak, 2),
         "seq_tokens_per_s": round(seqs_total / (t_step * 1e-3), 1),
@@ -495,7 +522,8 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
         "kv_gbs": round(tot_kv / (t_step * 1e-3) / 1e9, 2),
         "roofline": {
             "bound": "hbm",
-            "kernel": "pa_tma_mma_kernel" if path == 1 else "pa_generic_kernel",
+            "kernel": ("pa_prefix_kernel + pa_tma_mma_kernel (events span both)" if cascade
+                       else "pa_tma_mma_kernel" if path == 1 else "pa_generic_kernel"),
             "achieved": round(kern_gbs, 2),
             "peak": peak,
             "unit": "GB/s",
@@ -513,8 +541,11 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
             "ms_per_step": round(t_e2e, 5),
             "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h),
-            "api": "nxt_backend_run (libxllm_cuda_backend.so); per step one pinned H2D copy "
-                   "(Q, block tables, seq_lens) and one D2H copy of the output",
+            "api": ("nxt_paged_attention_prefix_ex (libxpa.so); per step one pinned H2D copy "
+                    "(Q, block tables, seq_lens, prefix groups) and one D2H copy of the output"
+                    if cascade else
+                    "nxt_backend_run (libxllm_cuda_backend.so); per step one pinned H2D copy "
+                    "(Q, block tables, seq_lens) and one D2H copy of the output"),
             "clocks": clocks_e2e,
         },
         "clocks": clocks,

@@ -238,6 +238,40 @@ int nxt_paged_attention_append_ex(
     int *device_status,
     nxt_stream_t stream);
 
+/* ── extension: shared-prefix (cascade) decode attention ────────────────
+ * For batches whose sequences share radix-tree prefixes (config 4): prefix
+ * group g lists its member sequences group_members[group_offsets[g] ..
+ * group_offsets[g+1]); every member b has prefix_pages[b] = P_g and the same
+ * first P_g block-table entries; sequences in no group have prefix_pages 0.
+ * A sequence is in at most one group and its seq_len covers its prefix.
+ * Results are those of nxt_paged_attention_ex on the same inputs; the shared
+ * pages are read once per group and KV head and multiplied with all members'
+ * queries as one tensor-core tile, the private pages as usual. Shapes the TMA
+ * path does not take run the plain path. max_group_size / max_prefix_pages
+ * bound the device arrays' contents (host values). For head sizes 64 and 128
+ * the shared-prefix kernel (persistent, on a few SMs) and the private-page
+ * kernel run at the same time on `stream` (programmatic dependent launch). */
+int nxt_paged_attention_prefix_ex(
+    void *out, const void *query,
+    const void *key_cache, const void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    const int *prefix_pages, const int *group_offsets, const int *group_members,
+    int num_groups, int max_group_size, int max_prefix_pages,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq,
+    int block_size, int dtype_size,
+    int64_t kv_block_stride, int64_t kv_head_stride,
+    int64_t num_blocks,
+    void *workspace, size_t workspace_bytes,
+    int *device_status,
+    nxt_stream_t stream);
+
+/* Workspace bytes a nxt_paged_attention_prefix_ex call with these sizes needs. */
+size_t nxt_paged_attention_prefix_workspace_size(
+    int num_seqs, int num_heads, int head_size, int num_kv_heads,
+    int max_num_blocks_per_seq, int block_size, int max_prefix_pages);
+
 /* ── extension: KV-head sharding with the output all-gather fused in ────
  * For P GPUs of one box, one process or thread per GPU. Rank r owns KV
  * heads [r*Hkv/P, (r+1)*Hkv/P) with their query heads (head_offset =
@@ -293,8 +327,9 @@ int nxt_paged_attention_sharded(
 
 /* extension — instrumentation for timing the attention kernel alone. The next
  * call made by this host thread records `before` on its stream immediately
- * before the main attention kernel and `after` immediately after it (ahead of
- * the split-context reduce). Both are cudaEvent_t values cast to void*; the
+ * before the main attention kernel (before the shared-prefix kernel of a
+ * cascade call) and `after` immediately after it (ahead of the split-context
+ * reduce). Both are cudaEvent_t values cast to void*; the
  * request is consumed by that one call. NULL, NULL cancels a pending request. */
 int nxt_paged_attention_profile_next(void *before, void *after);
 

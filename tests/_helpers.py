@@ -13,9 +13,13 @@ from xllms_b200 import workloads as W
 RTOL = 1e-3
 
 
-def oracle_out(batch: W.PagedBatch, q, k, v, num_blocks=-1) -> np.ndarray:
+def oracle_out(batch: W.PagedBatch, q, k, v, num_blocks=-1, f64=False) -> np.ndarray:
+    """The oracle's output; f64=True accumulates in fp64 (the exact reference
+    for contexts long enough that the fp32 oracle's own rounding is a sizeable
+    share of the tolerance)."""
     return O.attention(q, k, v, batch.block_tables, batch.seq_lens, batch.num_kv_heads,
-                       batch.scale, block_size=batch.block_size, num_blocks=num_blocks)
+                       batch.scale, block_size=batch.block_size, num_blocks=num_blocks,
+                       f64=f64)
 
 
 def to_device(batch: W.PagedBatch, q, k, v, dev):

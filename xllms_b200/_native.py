@@ -57,6 +57,12 @@ SIGNATURES = {
          _VP, _VP],
     ),
     "nxt_paged_attention_profile_next": (_I, [_VP, _VP]),
+    "nxt_paged_attention_prefix_ex": (
+        _I,
+        [_VP, _CVP, _CVP, _CVP, _IP, _IP, _IP, _IP, _IP, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,
+         _I, _I64, _I64, _I64, _VP, _SZ, _VP, _VP],
+    ),
+    "nxt_paged_attention_prefix_workspace_size": (_SZ, [_I, _I, _I, _I, _I, _I, _I]),
     "nxt_reshape_and_cache": (
         _I, [_CVP, _CVP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I64, _I64, _I64, _VP]),
     "nxt_paged_attention_append_ex": (

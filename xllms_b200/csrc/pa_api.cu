@@ -8,12 +8,15 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <utility>
 
 #include "operator_api.h"
 #include "pa_host.h"
 #include "pa_launch.h"
+#include "pa_prefix.h"
 
 namespace {
 
@@ -187,11 +190,47 @@ using namespace xpa::host;
 
 namespace {
 
+// Shared-prefix groups of a cascade call (device arrays, host sizes).
+struct PrefixArgs {
+  const int* prefix_pages;
+  const int* offsets;
+  const int* members;
+  int num_groups, max_group_size, max_prefix_pages;
+};
+
+#ifndef XPA_PREFIX_CTA_SCALE
+#define XPA_PREFIX_CTA_SCALE 2.0
+#endif
+// CTAs of the persistent shared-prefix kernel, which runs beside the suffix
+// kernel: enough that its estimated work (S blocks of 64 tokens x 128 rows at
+// ~1.2 us each on one SM) ends within the suffix kernel's estimated HBM time
+// (half the non-prefix pages of every sequence at 6 TB/s), at least 8.
+int prefix_ctas(int B, int Hq, int D, int Hkv, int max_blocks, int num_groups,
+                int max_group_size, int max_prefix_pages, int sm_count) {
+  const double blocks = (double)num_groups * Hkv * ceil_div((long long)max_group_size * (Hq / Hkv), 128) *
+                        ceil_div(max_prefix_pages, 4);
+  const double work_us = blocks * 1.2;
+  const double suffix_pages = std::max(1.0, 0.5 * (max_blocks - max_prefix_pages));
+  const double suffix_us =
+      std::max(1.0, (double)B * Hkv * suffix_pages * (16.0 * D * 2 * 2) / 6.0e6);
+  const int n = (int)std::ceil(XPA_PREFIX_CTA_SCALE * work_us / suffix_us);
+  return std::min(sm_count, std::max(8, n));
+}
+
+// Pages per prefix partial slot: short chunks, so the prefix kernel (one CTA
+// per chunk x block of query rows x KV head) has enough CTAs; at most 64
+// chunks while a chunk stays within the kernel's 512 pages.
+int prefix_chunk_pages(int max_prefix_pages) {
+  int cp = 16;
+  while (ceil_div(max_prefix_pages, cp) > 64 && cp < 512) cp <<= 1;
+  return cp;
+}
+
 int run(void* out, const void* q, const void* k, const void* v, const int* bt, const int* sl,
         int B, int Hq, int D, int Hkv, float scale, int max_blocks, int bs, int ds,
         long long kbs, long long khs, long long num_blocks, void* ws, size_t ws_bytes,
         int* dev_status, cudaStream_t st, const NxtPaShard* shard = nullptr,
-        uint64_t step = 0, bool after_append = false) {
+        uint64_t step = 0, bool after_append = false, const PrefixArgs* pre = nullptr) {
   if (shard) {
     if (shard->world_size < 1 || shard->world_size > NXT_PA_MAX_PEERS || shard->rank < 0 ||
         shard->rank >= shard->world_size || step == 0 || shard->head_offset < 0 ||
@@ -206,7 +245,26 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NXT_PA_ECUDA;
-  const Plan pl = make_plan(B, Hq, D, Hkv, max_blocks, sm_count_of(dev));
+  Plan pl = make_plan(B, Hq, D, Hkv, max_blocks, sm_count_of(dev));
+  // A cascade call needs the TMA path's shapes; others run without the prefix
+  // information, which gives the same result.
+  CUtensorMap tk, tv;
+  const bool fast = xpa::fast_path_shape_ok(D, Hq / Hkv, bs, ds) &&
+                    fast_layout_ok(k, v, D, Hkv, kbs, khs) &&
+                    (reinterpret_cast<uintptr_t>(q) & 3u) == 0 &&
+                    encode_pool(&tk, k, D, Hkv, num_blocks, kbs, khs) &&
+                    encode_pool(&tv, v, D, Hkv, num_blocks, kbs, khs);
+  if (pre && (!fast || pre->num_groups <= 0 || pre->max_prefix_pages <= 0 ||
+              pre->max_group_size <= 0))
+    pre = nullptr;
+  int slots = pl.max_parts, pchunk = 1, pchunks = 0;
+  if (pre) {
+    if (!pre->prefix_pages || !pre->offsets || !pre->members) return NXT_PA_EINVAL;
+    pchunk = prefix_chunk_pages(pre->max_prefix_pages);
+    pchunks = ceil_div(pre->max_prefix_pages, pchunk);
+    slots = pl.max_parts + pchunks;
+    pl.ws_bytes = (size_t)B * Hq * slots * (size_t)(D + 2) * sizeof(float);
+  }
   if ((long long)B * Hkv * pl.max_parts > INT_MAX || (long long)B * Hq > INT_MAX)
     return NXT_PA_EINVAL;
 
@@ -245,7 +303,7 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   p.block_tables = bt;
   p.seq_lens = sl;
   p.part_o = static_cast<float*>(part);
-  p.part_ml = part ? static_cast<float*>(part) + (size_t)B * Hq * pl.max_parts * D : nullptr;
+  p.part_ml = part ? static_cast<float*>(part) + (size_t)B * Hq * slots * D : nullptr;
   p.status = status;
   p.kv_block_stride = kbs;
   p.kv_head_stride = khs;
@@ -260,6 +318,9 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   p.block_size = bs;
   p.part_pages = pl.part_pages;
   p.max_parts = pl.max_parts;
+  p.slots = slots;
+  p.prefix_pages = pre ? pre->prefix_pages : nullptr;
+  p.prefix_chunk = pchunk;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.after_append = after_append ? 1 : 0;
   {
@@ -280,20 +341,44 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
     for (int r = 0; r < shard->world_size; ++r) p.peers[r] = shard->peer_out[r];
   }
 
-  cudaError_t e;
-  CUtensorMap tk, tv;
-  const bool fast = xpa::fast_path_shape_ok(D, p.GS, bs, ds) &&
-                    fast_layout_ok(k, v, D, Hkv, kbs, khs) &&
-                    (reinterpret_cast<uintptr_t>(q) & 3u) == 0 &&
-                    encode_pool(&tk, k, D, Hkv, num_blocks, kbs, khs) &&
-                    encode_pool(&tv, v, D, Hkv, num_blocks, kbs, khs);
   cudaEvent_t ev_a = g_prof_before, ev_b = g_prof_after;
   g_prof_before = g_prof_after = nullptr;
   if (ev_a && cudaEventRecord(ev_a, st) != cudaSuccess) return NXT_PA_ECUDA;
-  e = fast ? xpa::launch_fast(tk, tv, p, st) : xpa::launch_generic(p, ds, st);
-  if (e != cudaSuccess) return map_cuda(e);
+  cudaError_t e;
+  if (pre) {
+    xpa::PrefixGroups pg{};
+    pg.offsets = pre->offsets;
+    pg.members = pre->members;
+    pg.num_groups = pre->num_groups;
+    pg.max_group_size = pre->max_group_size;
+    pg.max_chunks = pchunks;
+    const int sms = sm_count_of(dev);
+    if (xpa::prefix_tc_ok(p)) {
+      // The persistent tcgen05 prefix kernel (compute-bound, one CTA per SM)
+      // takes a few SMs; the suffix kernel, launched as its programmatic
+      // dependent, starts at once and streams HBM on the others. CTA 0 of
+      // the suffix kernel waits for the prefix grid before exiting, so the
+      // merge (dependent of the suffix kernel) sees both.
+      const int ctas = prefix_ctas(B, Hq, D, Hkv, max_blocks, pre->num_groups,
+                                   pre->max_group_size, pre->max_prefix_pages, sms);
+      e = xpa::launch_prefix(tk, tv, p, pg, ctas, st);
+      if (e != cudaSuccess) return map_cuda(e);
+      xpa::Params ps = p;
+      ps.join_primary = 1;
+      e = xpa::launch_fast(tk, tv, ps, st);
+      if (e != cudaSuccess) return map_cuda(e);
+    } else {
+      e = xpa::launch_prefix(tk, tv, p, pg, sms, st);
+      if (e != cudaSuccess) return map_cuda(e);
+      e = xpa::launch_fast(tk, tv, p, st);
+      if (e != cudaSuccess) return map_cuda(e);
+    }
+  } else {
+    e = fast ? xpa::launch_fast(tk, tv, p, st) : xpa::launch_generic(p, ds, st);
+    if (e != cudaSuccess) return map_cuda(e);
+  }
   if (ev_b && cudaEventRecord(ev_b, st) != cudaSuccess) return NXT_PA_ECUDA;
-  if (pl.max_parts > 1) {
+  if (pl.max_parts > 1 || pre) {
     e = xpa::launch_reduce(p, ds, st);
     if (e != cudaSuccess) return map_cuda(e);
   }
@@ -445,6 +530,40 @@ int nxt_paged_attention_release_workspaces(void) {
   }
   if (have_prev) cudaSetDevice(prev);
   return rc;
+}
+
+int nxt_paged_attention_prefix_ex(void* out, const void* query, const void* key_cache,
+                                  const void* value_cache, const int* block_tables,
+                                  const int* seq_lens, const int* prefix_pages,
+                                  const int* group_offsets, const int* group_members,
+                                  int num_groups, int max_group_size, int max_prefix_pages,
+                                  int num_seqs, int num_heads, int head_size, int num_kv_heads,
+                                  float scale, int max_num_blocks_per_seq, int block_size,
+                                  int dtype_size, int64_t kv_block_stride, int64_t kv_head_stride,
+                                  int64_t num_blocks, void* workspace, size_t workspace_bytes,
+                                  int* device_status, nxt_stream_t stream) {
+  if (num_groups < 0 || max_group_size < 0 || max_prefix_pages < 0) return NXT_PA_EINVAL;
+  PrefixArgs pre{prefix_pages, group_offsets, group_members, num_groups, max_group_size,
+                 max_prefix_pages};
+  return run(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads,
+             head_size, num_kv_heads, scale, max_num_blocks_per_seq, block_size, dtype_size,
+             kv_block_stride, kv_head_stride, num_blocks, workspace, workspace_bytes,
+             device_status, static_cast<cudaStream_t>(stream), nullptr, 0, false, &pre);
+}
+
+size_t nxt_paged_attention_prefix_workspace_size(int num_seqs, int num_heads, int head_size,
+                                                 int num_kv_heads, int max_num_blocks_per_seq,
+                                                 int block_size, int max_prefix_pages) {
+  (void)block_size;
+  if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0 || head_size <= 0) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  const Plan pl = make_plan(num_seqs, num_heads, head_size, num_kv_heads, max_num_blocks_per_seq,
+                            sm_count_of(dev));
+  const int pchunks =
+      max_prefix_pages > 0 ? ceil_div(max_prefix_pages, prefix_chunk_pages(max_prefix_pages)) : 0;
+  return (size_t)num_seqs * num_heads * (pl.max_parts + pchunks) * (size_t)(head_size + 2) *
+         sizeof(float);
 }
 
 int nxt_reshape_and_cache(const void* key, const void* value, void* key_cache, void* value_cache,

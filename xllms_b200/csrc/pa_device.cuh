@@ -24,8 +24,8 @@ struct Params {
   const void* v;          // paged pool
   const int* block_tables;  // [B][max_blocks]
   const int* seq_lens;      // [B]
-  float* part_o;   // [B][Hq][max_parts][D] unnormalised partial outputs
-  float* part_ml;  // [B][Hq][max_parts][2] (max in log2 units, sum of exp2)
+  float* part_o;   // [B][Hq][slots][D] unnormalised partial outputs
+  float* part_ml;  // [B][Hq][slots][2] (max in log2 units, sum of exp2)
   int* status;     // device status word (NXT_PA_DEV_* bits), may be null
   long long kv_block_stride;
   long long kv_head_stride;
@@ -34,6 +34,12 @@ struct Params {
   int B, Hq, Hkv, D, GS;
   int max_blocks, block_size;
   int part_pages, max_parts;
+  int slots;         // partial slots per (b, q head) row: max_parts (+ prefix chunks)
+  // Shared-prefix (cascade) calls: the first prefix_pages[b] pages of sequence
+  // b are covered by its prefix group's partials (slots [0, ceil(P/pp)));
+  // this launch's partitions then start after them. Null: no prefix.
+  const int* prefix_pages;
+  int prefix_chunk;  // pages per prefix partial slot (cascade calls)
   float scale_log2;  // scale * log2(e): scores live in the exp2 domain
   // Fused head gather (KV-head sharding over GPUs): when npeers > 0 every
   // output row (b, h) of this rank is stored into each peers[r] at element
@@ -48,6 +54,7 @@ struct Params {
   // append kernel: a sequence's last page may only be read after
   // griddepcontrol.wait (the appended token lives there).
   int after_append;
+  int join_primary;  // CTA 0 waits for the preceding grid before it exits
 };
 
 // KV append: token t's rows key/value[t*token_stride + h*D + d] go to the
@@ -69,13 +76,22 @@ struct Item {
   int L;            // clamped context length of sequence b
   int page_begin;   // first page of this partition
   int page_end;     // one past its last page
-  int nparts;       // partitions of sequence b (0 when L == 0)
+  int nparts;       // partitions of sequence b after its prefix (0 when none)
+  int slot0;        // partial slot of partition 0 (= prefix chunks before it)
+  int direct;       // the item is the whole sequence: write the output itself
 };
 
 enum ItemKind { kItemNone = 0, kItemZero = 1, kItemWork = 2 };
 
 __device__ __forceinline__ void raise_status(const Params& p, int bits) {
   if (p.status) atomicOr(p.status, bits);
+}
+
+// Pages of sequence b (of npages) covered by its shared-prefix partials.
+__device__ __forceinline__ int prefix_of(const Params& p, int b, int npages) {
+  if (!p.prefix_pages) return 0;
+  const int P = __ldg(p.prefix_pages + b);
+  return P < 0 ? 0 : (P > npages ? npages : P);
 }
 
 // Grid index -> item. Index order is (b, kvh, part) with part fastest, so the
@@ -93,10 +109,13 @@ __device__ __forceinline__ ItemKind decode_item(const Params& p, int idx, Item& 
   }
   it.L = L;
   const int npages = (L + p.block_size - 1) / p.block_size;
-  it.nparts = (npages + p.part_pages - 1) / p.part_pages;
-  if (it.nparts == 0) return it.part == 0 ? kItemZero : kItemNone;
+  const int P = prefix_of(p, it.b, npages);
+  it.nparts = (npages - P + p.part_pages - 1) / p.part_pages;
+  it.slot0 = P > 0 ? (P + p.prefix_chunk - 1) / p.prefix_chunk : 0;
+  it.direct = (P == 0 && it.nparts == 1) ? 1 : 0;
+  if (it.nparts == 0) return (it.part == 0 && npages == 0) ? kItemZero : kItemNone;
   if (it.part >= it.nparts) return kItemNone;
-  it.page_begin = it.part * p.part_pages;
+  it.page_begin = P + it.part * p.part_pages;
   it.page_end = min(npages, it.page_begin + p.part_pages);
   return kItemWork;
 }
@@ -226,6 +245,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* tm,
       : "memory");
 }
 
+// Shared-memory byte offset of the 16-byte chunk `chunk` (along d) of token
+// row `tok` in a page tile written by TMA with 128-byte swizzle: the tile is
+// D/64 boxes of 16 rows x 128 bytes, and within each 1024-byte group the
+// chunk index is XORed with the row index mod 8.
+__device__ __forceinline__ uint32_t tile_off(int tok, int chunk) {
+  return (uint32_t)((chunk >> 3) * 2048 + tok * 128 + (((chunk & 7) ^ (tok & 7)) << 4));
+}
+
 // ── warp-level tensor-core fragments ────────────────────────────────────
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
                                         uint32_t& r3) {
@@ -346,134 +373,109 @@ __device__ __forceinline__ void store_out8(const Params& p, long long row, int d
   }
 }
 
-// ── split-context merge ─────────────────────────────────────────────────
-struct CtaSync {
-  __device__ __forceinline__ void operator()() const { __syncthreads(); }
-};
-
-// Log-sum-exp merge of the partials of one (b, q head) row into out:
-//   M = max_p m_p,  w_p = 2^(m_p - M),  out = sum_p w_p o_p / sum_p w_p l_p.
-// Run by `nthr` threads (index tid) that synchronise with sync(); `sm` is
-// shared scratch of cap + 34 floats (weights of the first `cap` partitions,
-// the rest recomputed). Partials were written by other CTAs of the same
-// launch, so they are read through L2 (ld.global.cg).
-template <typename T, typename Sync>
-__device__ __forceinline__ void merge_row(const Params& p, long long row, int nparts, int tid,
-                                          int nthr, float* sm, int cap, Sync sync) {
-  float* red = sm + cap;
-  const float* ml = p.part_ml + row * p.max_parts * 2;
-  const int lane = tid & 31, wid = tid >> 5, nw = (nthr + 31) >> 5;
-  float mx = -INFINITY;
-  for (int i = tid; i < nparts; i += nthr) mx = fmaxf(mx, __ldcg(ml + 2 * i));
-  mx = warp_max(mx);
-  if (lane == 0) red[wid] = mx;
-  sync();
-  float M = -INFINITY;
-  for (int w = 0; w < nw; ++w) M = fmaxf(M, red[w]);
-  float den = 0.f;
-  for (int i = tid; i < nparts; i += nthr) {
-    const float mp = __ldcg(ml + 2 * i);
-    const float wt = (M == -INFINITY || mp == -INFINITY) ? 0.f : ex2(mp - M);
-    if (i < cap) sm[i] = wt;
-    den = fmaf(wt, __ldcg(ml + 2 * i + 1), den);
-  }
-  den = warp_sum(den);
-  sync();  // every thread has read M from red[]
-  if (lane == 0) red[wid] = den;
-  sync();
-  float tot = 0.f;
-  for (int w = 0; w < nw; ++w) tot += red[w];
-  const float* po = p.part_o + row * p.max_parts * p.D;
-  if (p.vec8) {
-    for (int c = tid; c < p.D / 8; c += nthr) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int i = 0; i < nparts; ++i) {
-        float wt;
-        if (i < cap) {
-          wt = sm[i];
-        } else {
-          const float mp = __ldcg(ml + 2 * i);
-          wt = (M == -INFINITY || mp == -INFINITY) ? 0.f : ex2(mp - M);
-        }
-        const float4* src = reinterpret_cast<const float4*>(po + (long long)i * p.D + c * 8);
-        const float4 a = __ldcg(src), b = __ldcg(src + 1);
-        acc[0] = fmaf(wt, a.x, acc[0]);
-        acc[1] = fmaf(wt, a.y, acc[1]);
-        acc[2] = fmaf(wt, a.z, acc[2]);
-        acc[3] = fmaf(wt, a.w, acc[3]);
-        acc[4] = fmaf(wt, b.x, acc[4]);
-        acc[5] = fmaf(wt, b.y, acc[5]);
-        acc[6] = fmaf(wt, b.z, acc[6]);
-        acc[7] = fmaf(wt, b.w, acc[7]);
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) acc[k] = tot > 0.f ? acc[k] / tot : 0.f;
-      store_out8<T>(p, row, c * 8, acc);
-    }
+// Stores elements d0 .. d0+3 of output row `row`: one 8-byte (fp16) or
+// 16-byte (fp32) store per destination. Requires Params::vec8.
+template <typename T>
+__device__ __forceinline__ void store_out4(const Params& p, long long row, int d0, float4 v) {
+  long long off;
+  if (p.npeers == 0) {
+    off = row * p.D + d0;
   } else {
-    for (int d = tid; d < p.D; d += nthr) {
-      float acc = 0.f;
-      for (int i = 0; i < nparts; ++i) {
-        float wt;
-        if (i < cap) {
-          wt = sm[i];
-        } else {
-          const float mp = __ldcg(ml + 2 * i);
-          wt = (M == -INFINITY || mp == -INFINITY) ? 0.f : ex2(mp - M);
-        }
-        acc = fmaf(wt, __ldcg(po + (long long)i * p.D + d), acc);
-      }
-      store_out<T>(p, row, d, tot > 0.f ? acc / tot : 0.f);
-    }
+    const long long b = row / p.Hq, h = row - b * p.Hq;
+    off = p.peer_off + (b * p.Hq_total + p.head_offset + h) * p.D + d0;
   }
-  sync();  // sm and red are reused by the next row
+  if constexpr (sizeof(T) == 2) {
+    const uint2 u = make_uint2(pack_half2(v.x, v.y), pack_half2(v.z, v.w));
+    if (p.npeers == 0) {
+      *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + off) = u;
+      return;
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+      if (r < p.npeers) *reinterpret_cast<uint2*>(static_cast<__half*>(p.peers[r]) + off) = u;
+  } else {
+    if (p.npeers == 0) {
+      *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off) = v;
+      return;
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+      if (r < p.npeers) *reinterpret_cast<float4*>(static_cast<float*>(p.peers[r]) + off) = v;
+  }
 }
 
-// Merges the partials of the GS query heads (rows row0 .. row0+GS-1) of one
-// (sequence, KV head) at once: every
-// (head, partition) max and sum is staged in shared memory in one pass, the
-// weights of all heads are formed in parallel, and each output element then
-// needs nparts independent loads. Falls back to merge_row per head when the
-// staging does not fit in `cap` floats.
-template <typename T, typename Sync>
-__device__ __forceinline__ void merge_group(const Params& p, long long row0, int np, int tid,
-                                            int nthr, float* sm, int cap, Sync sync) {
-  const int GS = p.GS, D = p.D;
-  if (2 * GS * np + GS > cap) {
-    for (int h = 0; h < GS; ++h) merge_row<T>(p, row0 + h, np, tid, nthr, sm, cap, sync);
-    return;
+// ── split-context merge ─────────────────────────────────────────────────
+// Log-sum-exp merge of the partials (slots) of one (b, q head) row into out,
+// by one warp:
+//   M = max_i m_i,  w_i = 2^(m_i - M),  out = sum_i w_i o_i / sum_i w_i l_i.
+// Lane i holds slot i's (m, l) (slots past 32 are re-read from L2); the
+// weights of the first 32 slots go to the warp's 32 floats of shared memory
+// `sw`. Each lane then accumulates 4 consecutive output elements (1 without
+// vec8) over the slots, four slots' loads in flight at a time. Partials were
+// written by other CTAs, so they are read through L2 (ld.global.cg).
+template <typename T>
+__device__ __forceinline__ void merge_row_warp(const Params& p, long long row, int nslots,
+                                               int lane, float* sw) {
+  const float2* ml = reinterpret_cast<const float2*>(p.part_ml) + row * p.slots;
+  const float2 mine = lane < nslots ? __ldcg(ml + lane) : make_float2(-INFINITY, 0.f);
+  float mx = mine.x;
+  for (int i = lane + 32; i < nslots; i += 32) mx = fmaxf(mx, __ldcg(&ml[i].x));
+  const float M = warp_max(mx);
+  auto weight = [M](float m) { return (M == -INFINITY || m == -INFINITY) ? 0.f : ex2(m - M); };
+  const float wm = weight(mine.x);
+  sw[lane] = wm;
+  float den = wm * mine.y;
+  for (int i = lane + 32; i < nslots; i += 32) {
+    const float2 x = __ldcg(ml + i);
+    den = fmaf(weight(x.x), x.y, den);
   }
-  float* sw = sm;                // [GS][np]: maxima, then weights
-  float* sl = sm + GS * np;      // [GS][np]: sums
-  float* sinv = sl + GS * np;    // [GS]: 1 / merged sum
-  for (int e = tid; e < GS * np; e += nthr) {
-    const int h = e / np, i = e - h * np;
-    const float* ml = p.part_ml + ((row0 + h) * p.max_parts + i) * 2;
-    sw[e] = __ldcg(ml);
-    sl[e] = __ldcg(ml + 1);
-  }
-  sync();
-  for (int h = tid; h < GS; h += nthr) {
-    float M = -INFINITY;
-    for (int i = 0; i < np; ++i) M = fmaxf(M, sw[h * np + i]);
-    float den = 0.f;
-    for (int i = 0; i < np; ++i) {
-      const float m = sw[h * np + i];
-      const float wt = (M == -INFINITY || m == -INFINITY) ? 0.f : ex2(m - M);
-      sw[h * np + i] = wt;
-      den = fmaf(wt, sl[h * np + i], den);
+  const float tot = warp_sum(den);  // also orders sw[] for the whole warp
+  __syncwarp();
+  auto wt = [&](int i) { return i < 32 ? sw[i] : weight(__ldcg(&ml[i].x)); };
+  const float* po = p.part_o + row * p.slots * p.D;
+  if (p.vec8) {
+    for (int d0 = lane * 4; d0 < p.D; d0 += 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      int i = 0;
+      for (; i + 4 <= nslots; i += 4) {
+        float4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          x[u] = __ldcg(reinterpret_cast<const float4*>(po + (long long)(i + u) * p.D + d0));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float w = wt(i + u);
+          acc.x = fmaf(w, x[u].x, acc.x);
+          acc.y = fmaf(w, x[u].y, acc.y);
+          acc.z = fmaf(w, x[u].z, acc.z);
+          acc.w = fmaf(w, x[u].w, acc.w);
+        }
+      }
+      for (; i < nslots; ++i) {
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(po + (long long)i * p.D + d0));
+        const float w = wt(i);
+        acc.x = fmaf(w, x.x, acc.x);
+        acc.y = fmaf(w, x.y, acc.y);
+        acc.z = fmaf(w, x.z, acc.z);
+        acc.w = fmaf(w, x.w, acc.w);
+      }
+      if (tot > 0.f) {
+        acc.x /= tot;
+        acc.y /= tot;
+        acc.z /= tot;
+        acc.w /= tot;
+      } else {
+        acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      store_out4<T>(p, row, d0, acc);
     }
-    sinv[h] = den > 0.f ? 1.f / den : 0.f;
-  }
-  sync();
-  for (int e = tid; e < GS * D; e += nthr) {
-    const int h = e / D, d = e - h * D;
-    const float* po = p.part_o + (row0 + h) * p.max_parts * D + d;
-    const float* w = sw + h * np;
-    float acc = 0.f;
+  } else {
+    for (int d = lane; d < p.D; d += 32) {
+      float acc = 0.f;
 #pragma unroll 4
-    for (int i = 0; i < np; ++i) acc = fmaf(w[i], __ldcg(po + (long long)i * D), acc);
-    store_out<T>(p, row0 + h, d, acc * sinv[h]);
+      for (int i = 0; i < nslots; ++i) acc = fmaf(wt(i), __ldcg(po + (long long)i * p.D + d), acc);
+      store_out<T>(p, row, d, tot > 0.f ? acc / tot : 0.f);
+    }
   }
 }
 

@@ -131,10 +131,10 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
         }
       }
       const long long row = (long long)it.b * p.Hq + (long long)it.kvh * GS + hg0 + j;
-      if (it.nparts == 1) {
+      if (it.direct) {
         store_out<T>(p, row, d, den > 0.f ? num / den : 0.f);
       } else {
-        const long long pr = row * p.max_parts + it.part;
+        const long long pr = row * p.slots + it.slot0 + it.part;
         p.part_o[pr * D + d] = num;
         if (d == 0) {
           p.part_ml[2 * pr] = M;
@@ -160,14 +160,6 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
 // Each page of a KV head is read from HBM exactly once for all GS query heads.
 // ════════════════════════════════════════════════════════════════════════
 
-// Shared-memory byte offset of the 16-byte chunk `chunk` (along d) of token
-// row `tok` in a page tile written by TMA with 128-byte swizzle: the tile is
-// D/64 boxes of 16 rows x 128 bytes, and within each 1024-byte group the
-// chunk index is XORed with the row index mod 8.
-__device__ __forceinline__ uint32_t tile_off(int tok, int chunk) {
-  return (uint32_t)((chunk >> 3) * 2048 + tok * 128 + (((chunk & 7) ^ (tok & 7)) << 4));
-}
-
 // Bound on the producer's wait for its own in-flight copies after a timeout.
 constexpr uint64_t kDrainBudgetNs = 1000000000ull;
 
@@ -185,9 +177,8 @@ struct FastCfg {
 };
 
 template <int D, int NT, int STAGES, int NWC>
-__global__ void __launch_bounds__((NWC + 1) * 32)
-    pa_tma_mma_kernel(const __grid_constant__ CUtensorMap tmK,
-                      const __grid_constant__ CUtensorMap tmV, const Params p) {
+__device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUtensorMap& tmV,
+                                             const Params& p) {
   using C = FastCfg<D, NT, STAGES, NWC>;
   // Page j goes to stage j % STAGES and to consumer warp j % NWC. The parity
   // waits below are only sound when every stage always belongs to the same
@@ -478,7 +469,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
         num[7] = fmaf(wt, b.w, num[7]);
       }
     }
-    if (it.nparts == 1) {
+    if (it.direct) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) num[k] = den > 0.f ? num[k] / den : 0.f;
       if (p.vec8) {
@@ -488,7 +479,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
         for (int k = 0; k < 8; ++k) store_out<__half>(p, row0 + head, d0 + k, num[k]);
       }
     } else {
-      const long long pr = (row0 + head) * p.max_parts + it.part;
+      const long long pr = (row0 + head) * p.slots + it.slot0 + it.part;
       float* dst = p.part_o + pr * D + d0;
 #pragma unroll
       for (int k = 0; k < 8; ++k) dst[k] = num[k];
@@ -500,44 +491,46 @@ __global__ void __launch_bounds__((NWC + 1) * 32)
   }
 }
 
+template <int D, int NT, int STAGES, int NWC>
+__global__ void __launch_bounds__((NWC + 1) * 32)
+    pa_tma_mma_kernel(const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const Params p) {
+  tma_mma_body<D, NT, STAGES, NWC>(tmK, tmV, p);
+  // Beside a running shared-prefix grid: this grid may not complete before
+  // that one has (the merge after it reads both grids' partials).
+  if (p.join_primary && blockIdx.x == 0) pdl_wait_primary();
+}
+
 // ════════════════════════════════════════════════════════════════════════
-// Log-sum-exp reduce of split-context partials:
+// Log-sum-exp reduce of split-context partials (and shared-prefix chunks):
 //   M = max_p m_p,  w_p = 2^(m_p - M),  out = sum_p w_p o_p / sum_p w_p l_p
-// XPA_REDUCE_GROUPED 0: one CTA per (b, q head) row (merge_row);
-//                    1: one CTA per (b, KV head), its GS rows together.
+// One warp per (b, q head) row, 4 rows per CTA (merge_row_warp).
 // ════════════════════════════════════════════════════════════════════════
-#ifndef XPA_REDUCE_GROUPED
-#define XPA_REDUCE_GROUPED 0
-#endif
-#ifndef XPA_REDUCE_PDL
-#define XPA_REDUCE_PDL 1
-#endif
 template <typename T>
-__global__ void __launch_bounds__(128) pa_reduce_kernel(const Params p, int cap) {
-  extern __shared__ float sm_w[];  // [cap + 34]
-#if XPA_REDUCE_GROUPED
-  const int b = blockIdx.x / p.Hkv, kvh = blockIdx.x % p.Hkv;
-#else
-  const long long row = blockIdx.x;
-  const int b = (int)(row / p.Hq);
-#endif
-  int L = __ldg(p.seq_lens + b);
-  const long long lim = (long long)p.max_blocks * p.block_size;
-  L = L < 0 ? 0 : ((long long)L > lim ? (int)lim : L);
-  const int npages = (L + p.block_size - 1) / p.block_size;
-  const int nparts = (npages + p.part_pages - 1) / p.part_pages;
+__global__ void __launch_bounds__(128) pa_reduce_kernel(const Params p) {
+  __shared__ float sw[4][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * 4 + warp;
+  int nslots = 0;
+  bool direct = true;
+  if (row < (long long)p.B * p.Hq) {
+    const int b = (int)(row / p.Hq);
+    int L = __ldg(p.seq_lens + b);
+    const long long lim = (long long)p.max_blocks * p.block_size;
+    L = L < 0 ? 0 : ((long long)L > lim ? (int)lim : L);
+    const int npages = (L + p.block_size - 1) / p.block_size;
+    const int P = prefix_of(p, b, npages);
+    const int nparts = (npages - P + p.part_pages - 1) / p.part_pages;
+    nslots = (P > 0 ? (P + p.prefix_chunk - 1) / p.prefix_chunk : 0) + nparts;
+    direct = P == 0 && nparts <= 1;  // written directly by the attention kernel
+  }
   pdl_launch_dependents();  // the gather barrier (if any) may be scheduled now
   // Every CTA waits for the attention grid, also those with nothing to merge:
   // this grid must not complete before the attention kernel has (later work
   // on the stream is ordered after this grid, not after that kernel).
   pdl_wait_primary();
-  if (nparts <= 1) return;
-#if XPA_REDUCE_GROUPED
-  merge_group<T>(p, (long long)b * p.Hq + (long long)kvh * p.GS, nparts, threadIdx.x,
-                 blockDim.x, sm_w, cap, CtaSync());
-#else
-  merge_row<T>(p, row, nparts, threadIdx.x, blockDim.x, sm_w, cap, CtaSync());
-#endif
+  if (direct) return;
+  merge_row_warp<T>(p, row, nslots, lane, sw[warp]);
 }
 
 // ════════════════════════════════════════════════════════════════════════
@@ -696,8 +689,8 @@ cudaError_t launch_fast_t(const CUtensorMap& tk, const CUtensorMap& tv, const Pa
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   if (e != cudaSuccess) return e;
   const long long grid = (long long)p.B * p.Hkv * p.max_parts;
-  return launch_ex(kern, (unsigned)grid, C::kThreads, C::kSmem, st, p.after_append != 0, tk, tv,
-                   p);
+  return launch_ex(kern, (unsigned)grid, C::kThreads, C::kSmem, st,
+                   p.after_append != 0 || p.join_primary != 0, tk, tv, p);
 }
 
 }  // namespace
@@ -727,28 +720,19 @@ cudaError_t launch_fast(const CUtensorMap& tk, const CUtensorMap& tv, const Para
 }
 
 cudaError_t launch_reduce(const Params& p, int dtype_size, cudaStream_t st) {
-#if XPA_REDUCE_GROUPED
-  // The (head, partition) maxima, sums and weights, when they fit in 48 KB
-  // (else merge_group falls back to merging row by row).
-  const long long want = 2LL * p.GS * p.max_parts + p.GS;
-  const unsigned grid = (unsigned)((long long)p.B * p.Hkv);
-#else
-  const long long want = p.max_parts;  // the row's partition weights
-  const unsigned grid = (unsigned)((long long)p.B * p.Hq);
-#endif
-  const int cap = (int)(want < 12 * 1024 - 34 ? want : 12 * 1024 - 34);
+  const long long rows = (long long)p.B * p.Hq;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3((unsigned)((rows + 3) / 4));
   cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = (size_t)(cap + 34) * sizeof(float);
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = XPA_REDUCE_PDL ? 1 : 0;
-  if (dtype_size == 4) return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<float>, p, cap);
-  return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<__half>, p, cap);
+  cfg.numAttrs = 1;
+  if (dtype_size == 4) return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<float>, p);
+  return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<__half>, p);
 }
 
 cudaError_t launch_append(const AppendParams& a, int dtype_size, cudaStream_t st) {

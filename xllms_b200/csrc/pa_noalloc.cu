@@ -102,6 +102,7 @@ extern "C" int nxt_paged_attention_noalloc(
   p.block_size = block_size;
   p.part_pages = pl.part_pages;
   p.max_parts = pl.max_parts;
+  p.slots = pl.max_parts;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.vec8 = (D % 8 == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) ? 1 : 0;
 

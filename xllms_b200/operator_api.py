@@ -300,3 +300,68 @@ def paged_attention_append(query, key_cache, value_cache, block_tables, seq_lens
     if rc != _native.NXT_PA_OK:
         raise PagedAttentionError(rc, "nxt_paged_attention_append_ex")
     return out
+
+
+# ── shared-prefix (cascade) attention ─────────────────────────────────────
+class PrefixGroups:
+    """Device arrays of nxt_paged_attention_prefix_ex, built once from a host
+    list of (member sequence ids, shared prefix pages) pairs."""
+
+    def __init__(self, groups, num_seqs, device=None, *, prefix_pages=None, offsets=None,
+                 members=None):
+        import torch
+        self.num_groups = len(groups)
+        self.max_group_size = max((len(m) for m, _ in groups), default=0)
+        self.max_prefix_pages = max((int(p) for _, p in groups), default=0)
+        if prefix_pages is None:
+            pp, off, mem = self.host_arrays(groups, num_seqs)
+            t = lambda x: torch.from_numpy(x).to(device)
+            prefix_pages, offsets, members = t(pp), t(off), t(mem)
+        self.prefix_pages, self.offsets, self.members = prefix_pages, offsets, members
+
+    @staticmethod
+    def host_arrays(groups, num_seqs):
+        """(prefix_pages [num_seqs], offsets [G+1], members [sum of sizes]) as int32."""
+        import numpy as np
+        pp = np.zeros(max(1, num_seqs), dtype=np.int32)
+        off = [0]
+        mem = []
+        for seqs, pages in groups:
+            for b in seqs:
+                if not 0 <= int(b) < num_seqs:
+                    raise ValueError(f"group member {b} outside the batch")
+                if pp[int(b)]:
+                    raise ValueError(f"sequence {b} is in two prefix groups")
+                pp[int(b)] = int(pages)
+            mem.extend(int(b) for b in seqs)
+            off.append(len(mem))
+        return (pp, np.asarray(off, dtype=np.int32),
+                np.asarray(mem if mem else [0], dtype=np.int32))
+
+
+def paged_attention_prefix(query, key_cache, value_cache, block_tables, seq_lens, groups, *,
+                           scale=None, out=None, num_blocks=None, device_status=None,
+                           stream=None):
+    """Decode attention for a batch with shared prefixes. `groups` is a
+    PrefixGroups or a host list of (member sequence ids, shared prefix pages);
+    every member's seq_len covers its prefix and its block-table row starts
+    with the group's shared pages. The result equals paged_attention's."""
+    import torch
+    B, Hq, D = query.shape
+    nb, Hkv, bs, _ = key_cache.shape
+    if not isinstance(groups, PrefixGroups):
+        groups = PrefixGroups(groups, B, query.device)
+    if out is None:
+        out = torch.empty_like(query)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    rc = _native.xpa().nxt_paged_attention_prefix_ex(
+        _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+        _ptr(seq_lens), _ptr(groups.prefix_pages), _ptr(groups.offsets), _ptr(groups.members),
+        groups.num_groups, groups.max_group_size, groups.max_prefix_pages, B, Hq, D, Hkv,
+        float(scale), block_tables.shape[1], bs, _dtype_size(query), Hkv * bs * D, bs * D,
+        nb if num_blocks is None else int(num_blocks), None, 0, _ptr(device_status),
+        _stream_ptr(stream))
+    if rc != _native.NXT_PA_OK:
+        raise PagedAttentionError(rc, "nxt_paged_attention_prefix_ex")
+    return out

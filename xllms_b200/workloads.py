@@ -44,6 +44,8 @@ class PagedBatch:
     rank: int = 0
     total_heads: int = 0    # query heads across all ranks
     notes: dict = field(default_factory=dict)
+    # shared radix prefixes: (member sequence ids, shared leading pages) per group
+    prefix_groups: list = field(default_factory=list)
 
     @property
     def group(self) -> int:
@@ -150,14 +152,15 @@ def _assign_pages(rng: np.random.Generator, lens: Sequence[int], block_size: int
                   max_blocks: int, slack: float, prefix: Optional[List[int]] = None,
                   prefix_of: Optional[Sequence[int]] = None) -> Tuple[np.ndarray, int]:
     """Block tables over one shuffled pool: shared prefix page sets first (if
-    any), then every sequence's private pages as disjoint consecutive slices."""
+    any), then every sequence's private pages as disjoint consecutive slices.
+    prefix_of[b] is the index of b's shared prefix in `prefix`, or -1."""
     B = len(lens)
     prefix = prefix or []
     prefix_pages = [p // block_size for p in prefix]
     priv = []
     for b in range(B):
         npg = (int(lens[b]) + block_size - 1) // block_size
-        shared = prefix_pages[prefix_of[b]] if prefix_of is not None else 0
+        shared = prefix_pages[prefix_of[b]] if prefix_of is not None and prefix_of[b] >= 0 else 0
         priv.append(npg - shared)
     used = sum(prefix_pages) + sum(priv)
     pool = max(1, int(math.ceil(used * (1.0 + slack))))
@@ -170,7 +173,7 @@ def _assign_pages(rng: np.random.Generator, lens: Sequence[int], block_size: int
         cur += npg
     for b in range(B):
         j = 0
-        if prefix_of is not None:
+        if prefix_of is not None and prefix_of[b] >= 0:
             ids = prefix_ids[prefix_of[b]]
             tables[b, :len(ids)] = ids
             j = len(ids)
@@ -198,11 +201,17 @@ def make_batch(name: str, lens: Sequence[int], num_heads: int, num_kv_heads: int
     ts = seed if table_seed is None else table_seed
     rng = np.random.default_rng([ts, 11, rank])
     tables, pool = _assign_pages(rng, lens, block_size, max_blocks, slack, prefix, prefix_of)
+    groups = []
+    if prefix and prefix_of is not None:
+        for gi, plen in enumerate(prefix):
+            seqs = [b for b in range(len(lens)) if prefix_of[b] == gi]
+            if seqs:
+                groups.append((seqs, plen // block_size))
     return PagedBatch(name=name, num_seqs=len(lens), num_heads=hq, num_kv_heads=hkv,
                       head_size=head_size, block_size=block_size, dtype=dtype, seq_lens=lens,
                       block_tables=tables, num_blocks=pool, value_std=value_std, seed=seed,
                       scale=1.0 / math.sqrt(head_size), world_size=world_size, rank=rank,
-                      total_heads=num_heads)
+                      total_heads=num_heads, prefix_groups=groups)
 
 
 def config1(seed: int = 1) -> PagedBatch:
