@@ -147,6 +147,20 @@ class ClockSampler:
         except Exception as exc:  # pragma: no cover - depends on the box
             self.err = f"nvidia-smi unavailable: {exc}"
 
+    def wait_ready(self, timeout_s: float = 5.0):
+        """Blocks until nvidia-smi has written its first sample (it takes a
+        few hundred ms to start), so that short timed regions get samples."""
+        if self.proc is None:
+            return
+        t_end = time.time() + timeout_s
+        while time.time() < t_end:
+            try:
+                if os.path.getsize(self.tmp.name) > 0:
+                    return
+            except OSError:
+                return
+            time.sleep(0.02)
+
     @staticmethod
     def now():
         import datetime as _dt
@@ -331,6 +345,7 @@ def run_ours(args, rank, world, local_rank):
 
     # rank 0 samples its own GPU; every rank runs the same work in lockstep
     sampler = ClockSampler([local_rank], enabled=(rank == 0))
+    sampler.wait_ready()
     for _ in range(args.warmup):
         step()
     barrier()
