@@ -45,7 +45,14 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "act"], default="c2",
+                    help="c1..c5: the paged-attention configurations; act: one activation "
+                         "operator (--act-op) on a Llama-3-8B MLP-sized input, 1 GPU")
+    ap.add_argument("--act-op", default="silu_and_mul",
+                    choices=["silu_and_mul", "mul_and_silu", "gelu_and_mul",
+                             "gelu_tanh_and_mul", "gelu", "silu"])
+    ap.add_argument("--act-tokens", type=int, default=8192)
+    ap.add_argument("--act-d", type=int, default=14336)
     ap.add_argument("--cpu-seconds", type=float, default=6.0,
                     help="wall-time budget of the cpu_baseline leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -607,8 +614,110 @@ def run_reference(args, rank, world):
     }
 
 
+def run_activation(args):
+    """One activation operator on a [tokens, 2 d] fp16 input (Llama-3-8B MLP:
+    d = 14336): algorithmic bytes = input + output; roofline HBM."""
+    import torch
+    from oracle import oracle as O
+    from xllms_b200 import _native
+    from xllms_b200 import operator_api as PA
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    op = PA.ACTIVATIONS[args.act_op]
+    gated = op <= _native.NXT_ACT_GELU_TANH_AND_MUL
+    T, d = args.act_tokens, args.act_d
+    width = 2 * d if gated else d
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)
+    x = (torch.randn(T, width, generator=g, device=dev) * 2).to(torch.float16)
+    out = torch.empty(T, d, dtype=torch.float16, device=dev)
+    nbytes = (x.numel() + out.numel()) * 2
+    step = lambda: PA.activation(args.act_op, x, out=out)
+    sampler = ClockSampler([0])
+    sampler.wait_ready()
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    K = args.steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0 = ClockSampler.now()
+    e0.record()
+    for _ in range(K):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    c1 = ClockSampler.now()
+    t_step = e0.elapsed_time(e1) / K
+    # e2e: the input from pinned host memory, the output back, every step
+    x_h = x.cpu().pin_memory()
+    out_h = torch.empty(T, d, dtype=torch.float16).pin_memory()
+    x_d = torch.empty_like(x)
+
+    def e2e():
+        x_d.copy_(x_h, non_blocking=True)
+        PA.activation(args.act_op, x_d, out=out)
+        out_h.copy_(out, non_blocking=True)
+    for _ in range(3):
+        e2e()
+    torch.cuda.synchronize()
+    E = max(1, K // 4)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(E):
+        e2e()
+    f1.record()
+    torch.cuda.synchronize()
+    t_e2e = f0.elapsed_time(f1) / E
+    sampler.close()
+    cpu = None
+    if not args.no_cpu_baseline:
+        rows = max(1, min(T, 64))
+        xs = x[:rows].cpu().numpy()
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 5.0) or n == 0:
+            O.activation(op, xs)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        cpu = {"value": round(rows * (width + d) * 2 / dt / 1e9, 3), "unit": "GB/s", "cores": 1,
+               "kind": "port", "sample": f"{rows} of {T} rows, oracle/act_oracle.c (libm, 1 thread)"}
+    peak, peak_src = hbm_peak()
+    gbs = nbytes / (t_step * 1e-3) / 1e9
+    line = {
+        "metric": f"activation {args.act_op} GB/s (% of HBM peak)",
+        "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 1, "steps": K, "warmup": args.warmup,
+        "ms_per_step": round(t_step, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic: N(0,1)*2 fp16 drawn on the device (torch CUDA generator)",
+        "config": {"workload": f"act_{args.act_op}", "tokens": T, "d": d,
+                   "input": f"[{T}, {width}] fp16", "output": f"[{T}, {d}] fp16",
+                   "l2": f"no flush: {nbytes / 1e6:.0f} MB per step (> {L2_BYTES >> 20} MB L2)"},
+        "pct_hbm_peak": round(100.0 * gbs / peak, 2),
+        "roofline": {"bound": "hbm", "kernel": "act_vec_kernel", "achieved": round(gbs, 2),
+                     "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
+                     "bytes_per_launch": nbytes, "traffic": None},
+        "e2e": {"value": round(nbytes / (t_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(t_e2e, 5), "h2d_bytes_per_step": x.numel() * 2,
+                "d2h_bytes_per_step": out.numel() * 2,
+                "api": "nxt_activation_ex (libxpa.so), pinned host buffers"},
+        "clocks": sampler.summary(c0, c1),
+        "gpu_launches": K,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
 def main():
     args = parse_args()
+    if args.workload == "act":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the activation workload has no reference CPU arm"}), flush=True)
+            return
+        print(json.dumps(run_activation(args)), flush=True)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -238,6 +238,51 @@ int nxt_paged_attention_append_ex(
     int *device_status,
     nxt_stream_t stream);
 
+/* ═══════════════════════════════════════════════════════════════════════
+ * Activation + gating kernels (reference include/operator_api.h:121-150,
+ * operators/activation_kernels.cu). Row t of `input` is [gate (d) | up (d)]
+ * for the gated ops and d wide for the element-wise ones; `out` rows are d.
+ * dtype_size 2 = fp16, 4 = fp32, for input and out alike. The activation is
+ * computed in fp32 (expf / erff / tanhf), rounded to the storage type, and
+ * multiplied by the other half in the storage type, as in the reference.
+ * The drop-in entry points return nothing (like the reference) and record
+ * their status for nxt_activation_last_error.
+ * ═══════════════════════════════════════════════════════════════════════ */
+
+/** out = silu(gate) * up   (gate = first half of input) */
+void nxt_silu_and_mul(void *out, const void *input, int num_tokens, int d, int dtype_size,
+                      nxt_stream_t stream);
+/** out = gate * silu(up)   (up = second half of input) */
+void nxt_mul_and_silu(void *out, const void *input, int num_tokens, int d, int dtype_size,
+                      nxt_stream_t stream);
+/** out = gelu(gate) * up */
+void nxt_gelu_and_mul(void *out, const void *input, int num_tokens, int d, int dtype_size,
+                      nxt_stream_t stream);
+/** out = gelu_tanh(gate) * up */
+void nxt_gelu_tanh_and_mul(void *out, const void *input, int num_tokens, int d, int dtype_size,
+                           nxt_stream_t stream);
+/** out = GELU(input)  (element-wise) */
+void nxt_gelu_elementwise(void *out, const void *input, int num_tokens, int d, int dtype_size,
+                          nxt_stream_t stream);
+/** out = SiLU(input)  (element-wise) */
+void nxt_silu_elementwise(void *out, const void *input, int num_tokens, int d, int dtype_size,
+                          nxt_stream_t stream);
+
+#define NXT_ACT_SILU_AND_MUL      0
+#define NXT_ACT_MUL_AND_SILU      1
+#define NXT_ACT_GELU_AND_MUL      2
+#define NXT_ACT_GELU_TANH_AND_MUL 3
+#define NXT_ACT_GELU              4
+#define NXT_ACT_SILU              5
+
+/* extension — any of the six ops by code, returning NXT_PA_OK or a negative
+ * code (EINVAL: unknown op, d <= 0, num_tokens < 0, dtype, NULL pointer). */
+int nxt_activation_ex(int op, void *out, const void *input, int num_tokens, int d,
+                      int dtype_size, nxt_stream_t stream);
+
+/* extension — status of the calling thread's last drop-in activation call. */
+int nxt_activation_last_error(void);
+
 /* ── extension: shared-prefix (cascade) decode attention ────────────────
  * For batches whose sequences share radix-tree prefixes (config 4): prefix
  * group g lists its member sequences group_members[group_offsets[g] ..

@@ -52,12 +52,46 @@ def oracle_lib() -> ctypes.CDLL:
                                                     _I64, _I64, _I64]
         lib.pa_gather_mix.restype = ctypes.c_uint64
         lib.pa_gather_mix.argtypes = [ctypes.c_uint64] * 3
+        lib.act_oracle.restype = _I
+        lib.act_oracle.argtypes = [_I, _P, _P, _I, _I, _I]
         lib.pa_half_to_float.restype = _F
         lib.pa_half_to_float.argtypes = [ctypes.c_uint16]
         lib.pa_float_to_half.restype = ctypes.c_uint16
         lib.pa_float_to_half.argtypes = [_F]
         _oracle = lib
     return _oracle
+
+
+def activation(op: int, x: np.ndarray) -> np.ndarray:
+    """The activation oracle on x [rows, 2d] (gated ops 0-3) or [rows, d]
+    (element-wise ops 4, 5); fp16 or fp32, result in x's dtype."""
+    x = np.ascontiguousarray(x)
+    rows, width = x.shape
+    d = width // 2 if op <= 3 else width
+    out = np.zeros((rows, d), dtype=x.dtype)
+    rc = oracle_lib().act_oracle(int(op), _c(out), _c(x), rows, d, x.dtype.itemsize)
+    if rc != 0:
+        raise ValueError("activation oracle rejected the arguments")
+    return out
+
+
+REF_ACT_SO = os.path.join(HERE, "_ref", "libxllm_ref_act.so")
+_ref_act = None
+
+
+def ref_act_available() -> bool:
+    return os.path.exists(REF_ACT_SO)
+
+
+def ref_act_lib() -> ctypes.CDLL:
+    """The reference's own activation kernels (GPU), built by oracle/Makefile."""
+    global _ref_act
+    if _ref_act is None:
+        lib = ctypes.CDLL(REF_ACT_SO)
+        lib.ref_activation.restype = _I
+        lib.ref_activation.argtypes = [_I, _P, _P, _I, _I, _I, _P]
+        _ref_act = lib
+    return _ref_act
 
 
 def ref_available() -> bool:

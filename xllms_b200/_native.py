@@ -29,6 +29,12 @@ NXT_PA_DEV_SEQ_CLAMPED = 0x4
 NXT_PA_PATH_NONE = 0
 NXT_PA_PATH_TMA_MMA = 1
 NXT_PA_PATH_GENERIC = 2
+NXT_ACT_SILU_AND_MUL = 0
+NXT_ACT_MUL_AND_SILU = 1
+NXT_ACT_GELU_AND_MUL = 2
+NXT_ACT_GELU_TANH_AND_MUL = 3
+NXT_ACT_GELU = 4
+NXT_ACT_SILU = 5
 NXT_PA_MAX_PEERS = 8
 NXT_PA_IPC_HANDLE_BYTES = 64
 
@@ -57,6 +63,14 @@ SIGNATURES = {
          _VP, _VP],
     ),
     "nxt_paged_attention_profile_next": (_I, [_VP, _VP]),
+    "nxt_silu_and_mul": (None, [_VP, _CVP, _I, _I, _I, _VP]),
+    "nxt_mul_and_silu": (None, [_VP, _CVP, _I, _I, _I, _VP]),
+    "nxt_gelu_and_mul": (None, [_VP, _CVP, _I, _I, _I, _VP]),
+    "nxt_gelu_tanh_and_mul": (None, [_VP, _CVP, _I, _I, _I, _VP]),
+    "nxt_gelu_elementwise": (None, [_VP, _CVP, _I, _I, _I, _VP]),
+    "nxt_silu_elementwise": (None, [_VP, _CVP, _I, _I, _I, _VP]),
+    "nxt_activation_ex": (_I, [_I, _VP, _CVP, _I, _I, _I, _VP]),
+    "nxt_activation_last_error": (_I, []),
     "nxt_paged_attention_prefix_ex": (
         _I,
         [_VP, _CVP, _CVP, _CVP, _IP, _IP, _IP, _IP, _IP, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,

@@ -365,3 +365,38 @@ def paged_attention_prefix(query, key_cache, value_cache, block_tables, seq_lens
     if rc != _native.NXT_PA_OK:
         raise PagedAttentionError(rc, "nxt_paged_attention_prefix_ex")
     return out
+
+
+# ── activations (operators/activation_kernels.cu of the reference) ─────────
+ACTIVATIONS = {
+    "silu_and_mul": _native.NXT_ACT_SILU_AND_MUL,
+    "mul_and_silu": _native.NXT_ACT_MUL_AND_SILU,
+    "gelu_and_mul": _native.NXT_ACT_GELU_AND_MUL,
+    "gelu_tanh_and_mul": _native.NXT_ACT_GELU_TANH_AND_MUL,
+    "gelu": _native.NXT_ACT_GELU,
+    "silu": _native.NXT_ACT_SILU,
+}
+
+
+def activation(name, x, *, out=None, stream=None):
+    """Gated ops take x [..., 2d] ([gate | up]) and return [..., d]; the
+    element-wise ops (gelu, silu) keep x's shape. fp16 or fp32, contiguous."""
+    import torch
+    op = ACTIVATIONS[name]
+    if not x.is_contiguous():
+        raise ValueError("activation input must be contiguous")
+    gated = op <= _native.NXT_ACT_GELU_TANH_AND_MUL
+    width = x.shape[-1]
+    if gated and width % 2:
+        raise ValueError("gated activation input needs an even last dimension")
+    d = width // 2 if gated else width
+    rows = x.numel() // width if width else 0
+    if out is None:
+        out = torch.empty(tuple(x.shape[:-1]) + (d,), dtype=x.dtype, device=x.device)
+    elif out.numel() != rows * d or out.dtype != x.dtype or not out.is_contiguous():
+        raise ValueError("activation output does not match the input")
+    rc = _native.xpa().nxt_activation_ex(op, _ptr(out), _ptr(x), rows, d, _dtype_size(x),
+                                         _stream_ptr(stream))
+    if rc != _native.NXT_PA_OK:
+        raise PagedAttentionError(rc, "nxt_activation_ex")
+    return out
