@@ -48,6 +48,9 @@ def parse_args():
     ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "act"], default="c2",
                     help="c1..c5: the paged-attention configurations; act: one activation "
                          "operator (--act-op) on a Llama-3-8B MLP-sized input, 1 GPU")
+    ap.add_argument("--kv", choices=["fp16", "e4m3", "e5m2"], default="fp16",
+                    help="KV cache format (c2/c3/c5, 1 GPU): e4m3 / e5m2 = fp8 pools with one "
+                         "scale per pool (nxt_paged_attention_fp8_ex)")
     ap.add_argument("--act-op", default="silu_and_mul",
                     choices=["silu_and_mul", "mul_and_silu", "gelu_and_mul",
                              "gelu_tanh_and_mul", "gelu", "silu"])
@@ -253,10 +256,14 @@ def cpu_leg(batch, arrays, seconds: float = 0.0, passes: int = 0, warmup: int = 
     import numpy as np
     from oracle import oracle as O
     q, k, v, bt, sl = arrays
+    if batch.kv_elem_size == 1:  # fp8 pools: the CPU path reads the dequantised values
+        fmt = O.FP8_E4M3 if batch.notes["kv_format"] == "e4m3" else O.FP8_E5M2
+        k = O.fp8_decode(k, fmt) * np.float32(batch.notes["k_scale"])
+        v = O.fp8_decode(v, fmt) * np.float32(batch.notes["v_scale"])
     nseq = len(sl)
     cores = host_cores()
     sub_bytes = int(sl.astype(np.int64).sum()) * batch.num_kv_heads * \
-        batch.head_size * 2 * batch.elem_size
+        batch.head_size * 2 * batch.kv_es
     sub_bytes += 2 * nseq * batch.num_heads * batch.head_size * batch.elem_size
     sub_bytes += int(((sl.astype(np.int64) + 15) // 16).sum()) * 4 + 4 * nseq
     if O.ref_available():
@@ -304,7 +311,13 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     batch = make_batch(args.workload, world, rank, args.seqs)
-    q, k, v = batch.values_torch(dev)
+    fp8 = args.kv != "fp16"
+    if fp8 and (world > 1 or args.workload in ("c1", "c4")):
+        raise SystemExit("--kv fp8 runs configs 2, 3 and 5 on one GPU")
+    if fp8:
+        q, k, v, k_scale, v_scale = batch.values_torch_fp8(dev, args.kv)
+    else:
+        q, k, v = batch.values_torch(dev)
     bt, sl = batch.tables_torch(dev)
     out = torch.empty_like(q)
     gathered = full = fg = None
@@ -339,6 +352,10 @@ def run_ours(args, rank, world, local_rank):
         if cascade:
             PA.paged_attention_prefix(q, k, v, bt, sl, groups, out=out,
                                       num_blocks=batch.num_blocks)
+            return
+        if fp8:
+            PA.paged_attention_fp8(q, k, v, bt, sl, args.kv, k_scale, v_scale, out=out,
+                                   num_blocks=batch.num_blocks)
             return
         PA.paged_attention(q, k, v, bt, sl, out=out, num_blocks=batch.num_blocks)
         if world > 1:
@@ -427,8 +444,8 @@ def run_ours(args, rank, world, local_rank):
     res = full if (world > 1 and not fused) else out_d
     out_h = torch.empty((batch.num_seqs, batch.total_heads, batch.head_size),
                         dtype=out.dtype).pin_memory()
-    pa_in = PA.make_input(q_d, k, v, bt_d, sl_d, scale=batch.scale,
-                          stream=torch.cuda.current_stream())
+    pa_in = None if fp8 else PA.make_input(q_d, k, v, bt_d, sl_d, scale=batch.scale,
+                                           stream=torch.cuda.current_stream())
 
     def e2e_step():
         stage_d.copy_(stage_h, non_blocking=True)
@@ -441,6 +458,10 @@ def run_ours(args, rank, world, local_rank):
             # the C-ABI cascade entry point (the plugin descriptor has no group fields)
             PA.paged_attention_prefix(q_d, k, v, bt_d, sl_d, groups_d, out=out_d,
                                       num_blocks=batch.num_blocks)
+        elif fp8:
+            # the C-ABI fp8 entry point (the plugin descriptor has no KV format)
+            PA.paged_attention_fp8(q_d, k, v, bt_d, sl_d, args.kv, k_scale, v_scale, out=out_d,
+                                   num_blocks=batch.num_blocks)
         elif plugin.run(pa_in, out_d) != 0:
             raise SystemExit("nxt_backend_run failed")
         if world > 1:
@@ -515,9 +536,12 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f16",
+        "dtype": "f16" if batch.kv_elem_size != 1 else
+                 f"f16 (Q, out), fp8 {batch.notes['kv_format']} KV",
         "data": "synthetic: seeded block tables/lengths (numpy PCG64); Q/K/V N(0,1)*std "
-                "drawn on the device (torch CUDA generator)",
+                "drawn on the device (torch CUDA generator)" +
+                ("; K/V quantised to fp8 with one scale per pool" if batch.kv_elem_size == 1
+                 else ""),
         "config": {
             "workload": batch.name,
             "num_seqs": batch.num_seqs,
@@ -536,7 +560,9 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
             "l2": f"no flush: each step reads {tot_kv / world / 1e9:.2f} GB of KV per GPU "
                   f"(> {L2_BYTES >> 20} MB L2)",
             "path": {1: "tma_mma", 2: "generic"}.get(path, "none") +
-                    (" + shared-prefix (cascade) kernel" if cascade else ""),
+                    (" + shared-prefix (cascade) kernel" if cascade else "") +
+                    (" (fp8 KV variant)" if batch.kv_elem_size == 1 else ""),
+            "kv_cache": batch.notes.get("kv_format", "fp16"),
         },
         "pct_hbm_peak": round(100.0 * (tot_ub / world) / (t_step * 1e-3) / 1e9 / peak, 2),
         "seq_tokens_per_s": round(seqs_total / (t_step * 1e-3), 1),
@@ -566,6 +592,9 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
             "api": ("nxt_paged_attention_prefix_ex (libxpa.so); per step one pinned H2D copy "
                     "(Q, block tables, seq_lens, prefix groups) and one D2H copy of the output"
                     if cascade else
+                    "nxt_paged_attention_fp8_ex (libxpa.so); per step one pinned H2D copy "
+                    "(Q, block tables, seq_lens) and one D2H copy of the output"
+                    if batch.kv_elem_size == 1 else
                     "nxt_backend_run (libxllm_cuda_backend.so); per step one pinned H2D copy "
                     "(Q, block tables, seq_lens) and one D2H copy of the output"),
             "clocks": clocks_e2e,

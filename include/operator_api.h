@@ -238,6 +238,90 @@ int nxt_paged_attention_append_ex(
     int *device_status,
     nxt_stream_t stream);
 
+/* ── extension: fp8 KV cache (reference operators/cache.py:16-24 lists
+ * "fp8", "fp8_e4m3", "fp8_e5m2" cache dtypes; no kernel there reads them) ──
+ * The pools hold one byte per element, encode(x / k_scale) for K and
+ * encode(x / v_scale) for V; attention reads decode(byte) * scale. Query and
+ * output are fp16; strides are in elements (= bytes). Head sizes 128 and 256
+ * with page size 16 take the TMA + tensor-core path; every other shape the
+ * CUDA-core kernel. Results are those of nxt_paged_attention_ex over the
+ * dequantised cache. */
+#define NXT_KV_FP8_E4M3 1 /* 4 exponent bits, no infinities, max 448   */
+#define NXT_KV_FP8_E5M2 2 /* 5 exponent bits, max 57344                 */
+
+int nxt_paged_attention_fp8_ex(
+    void *out, const void *query,
+    const void *key_cache, const void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq, int block_size,
+    int kv_format, float k_scale, float v_scale,
+    int64_t kv_block_stride, int64_t kv_head_stride,
+    int64_t num_blocks,
+    void *workspace, size_t workspace_bytes,
+    int *device_status,
+    nxt_stream_t stream);
+
+/* KV append into fp8 pools: fp16 key/value rows ([num_tokens][num_kv_heads]
+ * [head_size] at token_stride) are stored at slot_mapping[t] as
+ * encode(x / scale), rounded to nearest even and saturated at the format's
+ * largest finite value (NaN stays NaN). */
+int nxt_reshape_and_cache_fp8(
+    const void *key, const void *value,
+    void *key_cache, void *value_cache,
+    const int64_t *slot_mapping, int num_tokens,
+    int num_kv_heads, int head_size, int block_size,
+    int kv_format, float k_scale, float v_scale,
+    int64_t kv_block_stride, int64_t kv_head_stride, int64_t token_stride,
+    nxt_stream_t stream);
+
+/* ── extension: block-table builder ─────────────────────────────────────
+ * The glue between a continuous-batching scheduler and these kernels (the
+ * reference's scheduler, src/core/scheduler.c:278-440, stops at the list of
+ * scheduled requests). Host inputs, CSR over the step's sequences:
+ *   page_offsets [num_seqs + 1], page_ids [page_offsets[num_seqs]]: each
+ *     sequence's physical pages in token order;
+ *   seq_lens [num_seqs]: context tokens, the newest one included;
+ *   prefix_node / prefix_pages [num_seqs] (both NULL, or both given): the
+ *     radix-tree node of a sequence's longest shared prefix (-1: none) and
+ *     the whole pages it covers.
+ * Outputs, in one caller-owned device buffer (16-byte aligned, at least
+ * nxt_block_tables_layout bytes; offsets from the same call):
+ *   NXT_BT_TABLES        int32 [num_seqs][max_blocks], -1 past a sequence's pages
+ *   NXT_BT_SEQ_LENS      int32 [num_seqs]
+ *   NXT_BT_SLOTS         int64 [num_seqs], page * block_size + slot of the
+ *                        newest token (the KV append's slot_mapping; -1 when
+ *                        seq_len is 0)
+ *   NXT_BT_PREFIX_PAGES, NXT_BT_GROUP_OFFSETS, NXT_BT_GROUP_MEMBERS: the
+ *     prefix groups of nxt_paged_attention_prefix_ex — sequences sharing a
+ *     node with >= 1 whole page, groups of two or more; *num_groups,
+ *     *max_group_size and *max_prefix_pages receive its host bounds.
+ * The host packs the inputs into host_staging (pinned, at least
+ * nxt_block_tables_staging_size bytes; NULL: a temporary, and the call
+ * synchronises the stream) and issues one host-to-device copy and one
+ * kernel. EINVAL: a row longer than max_blocks, seq_len beyond its pages, a
+ * group whose members differ in shared page count or ids. */
+#define NXT_BT_TABLES        0
+#define NXT_BT_SEQ_LENS      1
+#define NXT_BT_SLOTS         2
+#define NXT_BT_PREFIX_PAGES  3
+#define NXT_BT_GROUP_OFFSETS 4
+#define NXT_BT_GROUP_MEMBERS 5
+#define NXT_BT_NUM_ARRAYS    6
+
+size_t nxt_block_tables_layout(int num_seqs, int max_blocks_per_seq, int total_pages,
+                               size_t offsets[NXT_BT_NUM_ARRAYS]);
+size_t nxt_block_tables_staging_size(int num_seqs, int total_pages);
+int nxt_build_block_tables(
+    const int *page_offsets, const int *page_ids, const int *seq_lens,
+    const int *prefix_node, const int *prefix_pages,
+    int num_seqs, int max_blocks_per_seq, int block_size,
+    void *device_buffer, size_t device_bytes,
+    void *host_staging, size_t staging_bytes,
+    int *num_groups, int *max_group_size, int *max_prefix_pages,
+    nxt_stream_t stream);
+
 /* ═══════════════════════════════════════════════════════════════════════
  * Activation + gating kernels (reference include/operator_api.h:121-150,
  * operators/activation_kernels.cu). Row t of `input` is [gate (d) | up (d)]

@@ -52,6 +52,10 @@ def oracle_lib() -> ctypes.CDLL:
                                                     _I64, _I64, _I64]
         lib.pa_gather_mix.restype = ctypes.c_uint64
         lib.pa_gather_mix.argtypes = [ctypes.c_uint64] * 3
+        lib.pa_fp8_decode.restype = None
+        lib.pa_fp8_decode.argtypes = [_P, _P, _I64, _I]
+        lib.pa_fp8_encode.restype = None
+        lib.pa_fp8_encode.argtypes = [_P, _P, _I64, _I]
         lib.act_oracle.restype = _I
         lib.act_oracle.argtypes = [_I, _P, _P, _I, _I, _I]
         lib.pa_half_to_float.restype = _F
@@ -149,6 +153,80 @@ def attention(q, k, v, block_tables, seq_lens, num_kv_heads, scale, block_size=1
     if rc != 0:
         raise ValueError("oracle rejected the arguments")
     return out
+
+
+def build_block_tables(page_offsets, page_ids, seq_lens, max_blocks, block_size=16,
+                       prefix_node=None, prefix_pages=None):
+    """Restatement of the block-table builder (xllms_b200/csrc/pa_tables.cu):
+    padded tables (-1), newest-token slots, and prefix groups (sequences
+    sharing a radix node with >= 1 whole page; groups of two or more, by
+    node id, members in sequence order). Returns (tables, slots,
+    prefix_pages_out, group_offsets, members, num_groups, max_group_size,
+    max_prefix_pages)."""
+    off = np.asarray(page_offsets, dtype=np.int64)
+    ids = np.asarray(page_ids, dtype=np.int64)
+    sl = np.asarray(seq_lens, dtype=np.int64)
+    B = len(sl)
+    tables = np.full((B, max_blocks), -1, dtype=np.int32)
+    slots = np.full(B, -1, dtype=np.int64)
+    for b in range(B):
+        row = ids[off[b]:off[b + 1]]
+        tables[b, :len(row)] = row
+        if sl[b] > 0:
+            slots[b] = row[(sl[b] - 1) // block_size] * block_size + (sl[b] - 1) % block_size
+    pp = np.zeros(B, dtype=np.int32)
+    go = np.zeros(B + 1, dtype=np.int32)
+    mem = np.zeros(B, dtype=np.int32)
+    G = nm = max_size = max_pages = 0
+    if prefix_node is not None:
+        nodes = {}
+        for b in range(B):
+            if prefix_node[b] >= 0 and prefix_pages[b] > 0:
+                nodes.setdefault(int(prefix_node[b]), []).append(b)
+        for node in sorted(nodes):
+            m = nodes[node]
+            if len(m) < 2:
+                continue
+            for b in m:
+                pp[b] = prefix_pages[m[0]]
+                mem[nm] = b
+                nm += 1
+            G += 1
+            go[G] = nm
+            max_size = max(max_size, len(m))
+            max_pages = max(max_pages, int(prefix_pages[m[0]]))
+        go[G + 1:] = nm
+    return tables, slots, pp, go, mem, G, max_size, max_pages
+
+
+FP8_E4M3, FP8_E5M2 = 1, 2
+
+
+def fp8_decode(codes, fmt) -> np.ndarray:
+    """uint8 codes -> float32 values (exact)."""
+    c = _as(codes, np.uint8)
+    out = np.zeros(c.shape, dtype=np.float32)
+    oracle_lib().pa_fp8_decode(_c(out), _c(c), c.size, int(fmt))
+    return out
+
+
+def fp8_encode(x, fmt) -> np.ndarray:
+    """float32 -> uint8 codes (round to nearest even, saturating)."""
+    x = _as(x, np.float32)
+    out = np.zeros(x.shape, dtype=np.uint8)
+    oracle_lib().pa_fp8_encode(_c(out), _c(x), x.size, int(fmt))
+    return out
+
+
+def attention_fp8(q, k_codes, v_codes, fmt, k_scale, v_scale, block_tables, seq_lens,
+                  num_kv_heads, scale, block_size=16, num_blocks=-1, f64=False) -> np.ndarray:
+    """Attention over an fp8 KV cache: K = decode(k_codes) * k_scale (V alike),
+    Q widened to fp32; then the same oracle as the fp16 / fp32 paths."""
+    k = fp8_decode(k_codes, fmt) * np.float32(k_scale)
+    v = fp8_decode(v_codes, fmt) * np.float32(v_scale)
+    q32 = np.asarray(q, dtype=np.float32)
+    return attention(q32, k, v, block_tables, seq_lens, num_kv_heads, scale,
+                     block_size=block_size, num_blocks=num_blocks, f64=f64)
 
 
 def split_partials(q, k, v, block_tables, seq_lens, num_kv_heads, scale, part_pages,

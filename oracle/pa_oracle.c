@@ -61,6 +61,62 @@ uint16_t pa_float_to_half(float x) {
     return sign | (uint16_t)h;
 }
 
+/* ── fp8 codecs (OCP 8-bit floating point: E4M3 without infinities, bias 7,
+ * max 448, 0x7F / 0xFF NaN; E5M2, bias 15, max 57344, IEEE-style inf/NaN) ── */
+static float fp8_decode_one(uint8_t c, int fmt) {
+    const int sign = c >> 7;
+    const int M = fmt == PA_FP8_E4M3 ? 3 : 2, bias = fmt == PA_FP8_E4M3 ? 7 : 15;
+    const int e = (c & 0x7f) >> M, m = c & ((1 << M) - 1);
+    float v;
+    if (fmt == PA_FP8_E4M3 && (c & 0x7f) == 0x7f) {
+        v = NAN;
+    } else if (fmt == PA_FP8_E5M2 && e == 31) {
+        v = m ? NAN : INFINITY;
+    } else if (e == 0) {
+        v = ldexpf((float)m, 1 - bias - M); /* subnormal */
+    } else {
+        v = ldexpf((float)((1 << M) + m), e - bias - M);
+    }
+    return sign ? -v : v;
+}
+
+/* Round to nearest even, saturating finite values (and infinities) at the
+ * largest finite magnitude; NaN stays NaN. */
+static uint8_t fp8_encode_one(float x, int fmt) {
+    const int M = fmt == PA_FP8_E4M3 ? 3 : 2, bias = fmt == PA_FP8_E4M3 ? 7 : 15;
+    const uint8_t max_code = fmt == PA_FP8_E4M3 ? 0x7e : 0x7b;
+    const uint8_t nan_code = 0x7f;
+    uint8_t sign = signbit(x) ? 0x80 : 0;
+    if (isnan(x)) return sign | nan_code;
+    if (isinf(x)) return sign | max_code;
+    const float a = fabsf(x);
+    const float min_normal = ldexpf(1.0f, 1 - bias);
+    uint32_t code;
+    if (a < min_normal) {
+        code = (uint32_t)nearbyintf(ldexpf(a, bias - 1 + M)); /* units of the subnormal step */
+    } else {
+        int e2;
+        const float fr = frexpf(a, &e2);                   /* a = fr * 2^e2, fr in [0.5, 1) */
+        const int e = e2 - 1;                               /* a = (2 fr) 2^e */
+        const float mant = ldexpf(2.0f * fr - 1.0f, M);     /* exact */
+        uint32_t m = (uint32_t)nearbyintf(mant);
+        int eb = e + bias;
+        if (m == (1u << M)) { m = 0; eb++; }
+        if (eb > 31) eb = 31;
+        code = ((uint32_t)eb << M) | m;
+    }
+    if (code > max_code) code = max_code;
+    return sign | (uint8_t)code;
+}
+
+void pa_fp8_decode(float *out, const uint8_t *in, int64_t n, int fmt) {
+    for (int64_t i = 0; i < n; i++) out[i] = fp8_decode_one(in[i], fmt);
+}
+
+void pa_fp8_encode(uint8_t *out, const float *in, int64_t n, int fmt) {
+    for (int64_t i = 0; i < n; i++) out[i] = fp8_encode_one(in[i], fmt);
+}
+
 static inline float load_f(const void *base, int64_t idx, int dtype_size) {
     if (dtype_size == 4) return ((const float *)base)[idx];
     return pa_half_to_float(((const uint16_t *)base)[idx]);

@@ -100,6 +100,16 @@ void pa_oracle_reshape_and_cache(const void *key, const void *value, void *key_c
                                  int elem_size, int64_t kv_block_stride,
                                  int64_t kv_head_stride, int64_t token_stride);
 
+/* fp8 formats of a quantised KV cache (fmt): 1 = E4M3 (no infinities, max
+ * 448, 0x7F NaN), 2 = E5M2 (max 57344). decode is exact; encode rounds to
+ * nearest even and saturates at the largest finite value (as the PTX
+ * cvt.rn.satfinite conversions do), NaN stays NaN. A quantised cache holds
+ * encode(x / scale) and reads back as decode(c) * scale. */
+#define PA_FP8_E4M3 1
+#define PA_FP8_E5M2 2
+void pa_fp8_decode(float *out, const uint8_t *in, int64_t n, int fmt);
+void pa_fp8_encode(uint8_t *out, const float *in, int64_t n, int fmt);
+
 /* Index-logic checksum: for every (seq, q head), the wrapping 64-bit sum of
  * pa_gather_mix(phys, slot, kv_head) over every token the attention reads. */
 uint64_t pa_gather_mix(uint64_t phys, uint64_t slot, uint64_t kv_head);

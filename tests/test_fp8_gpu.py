@@ -1,0 +1,106 @@
+"""fp8 KV cache on the GPU: attention over E4M3 / E5M2 pools equals the
+oracle over the dequantised pools (fp64 oracle), and
+the quantising append is bit-exact against the oracle's encoder."""
+import numpy as np
+import pytest
+
+from _helpers import check_close
+from oracle import oracle as O
+from xllms_b200 import _native
+from xllms_b200 import operator_api as PA
+from xllms_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+FMTS = [("e4m3", O.FP8_E4M3, 448.0), ("e5m2", O.FP8_E5M2, 57344.0)]
+EDGE_LENS = [0, 1, 15, 16, 17, 511, 512, 513, 1000]
+
+
+def _quantised(b, fmt, fmax):
+    q, k, v = b.values_numpy()
+    ks = float(np.abs(k.astype(np.float32)).max()) / fmax
+    vs = float(np.abs(v.astype(np.float32)).max()) / fmax
+    k8 = O.fp8_encode(k.astype(np.float32) / np.float32(ks), fmt)
+    v8 = O.fp8_encode(v.astype(np.float32) / np.float32(vs), fmt)
+    return q, k8, v8, ks, vs
+
+
+def _run(cuda, b, name, fmt, fmax, num_blocks=None):
+    import torch
+    q, k8, v8, ks, vs = _quantised(b, fmt, fmax)
+    ref = O.attention_fp8(q, k8, v8, fmt, ks, vs, b.block_tables, b.seq_lens, b.num_kv_heads,
+                          b.scale, block_size=b.block_size,
+                          num_blocks=-1 if num_blocks is None else num_blocks, f64=True)
+    bt, sl = b.tables_torch(cuda)
+    out = PA.paged_attention_fp8(torch.from_numpy(q).to(cuda), torch.from_numpy(k8).to(cuda),
+                                 torch.from_numpy(v8).to(cuda), bt, sl, name, ks, vs,
+                                 scale=b.scale, num_blocks=num_blocks)
+    torch.cuda.synchronize()
+    return out, ref
+
+
+@pytest.mark.parametrize("name,fmt,fmax", FMTS)
+@pytest.mark.parametrize("head_size", [64, 128, 256])
+@pytest.mark.parametrize("group", [1, 4, 8, 16])
+def test_fp8_attention(cuda, name, fmt, fmax, head_size, group):
+    if head_size == 256 and group > 8:
+        pytest.skip("D = 256 takes at most 8 heads per KV head on the fast path; covered below")
+    b = W.make_batch("f8", EDGE_LENS, 2 * group, 2, head_size, "f16", 300 + group, value_std=0.5)
+    out, ref = _run(cuda, b, name, fmt, fmax)
+    check_close(out, ref, what=f"{name} D={head_size} GS={group}")
+    assert PA.device_status() == 0
+
+
+@pytest.mark.parametrize("name,fmt,fmax", FMTS)
+def test_fp8_split_context_and_long(cuda, name, fmt, fmax):
+    b = W.make_batch("f8s", [20000, 3, 4097, 131], 16, 2, 128, "f16", 321, value_std=1.0)
+    out, ref = _run(cuda, b, name, fmt, fmax)
+    check_close(out, ref, what=f"{name} split")
+
+
+def test_fp8_d256_group16_generic(cuda):
+    b = W.make_batch("f8g", [300, 17], 32, 2, 256, "f16", 322)
+    out, ref = _run(cuda, b, "e4m3", O.FP8_E4M3, 448.0)
+    check_close(out, ref, what="D=256 GS=16")
+
+
+def test_fp8_other_page_size(cuda):
+    b = W.make_batch("f8p", [1, 31, 32, 33, 700], 8, 2, 128, "f16", 323, block_size=32)
+    out, ref = _run(cuda, b, "e5m2", O.FP8_E5M2, 57344.0)
+    check_close(out, ref, what="block_size 32")
+
+
+def test_fp8_bad_pages_masked(cuda):
+    b = W.make_batch("f8b", [200, 64, 90], 8, 2, 128, "f16", 324)
+    b.block_tables = b.block_tables.copy()
+    b.block_tables[0, 3] = -1
+    b.block_tables[2, 1] = b.num_blocks + 5
+    PA.device_status(clear=True)
+    out, ref = _run(cuda, b, "e4m3", O.FP8_E4M3, 448.0, num_blocks=b.num_blocks)
+    check_close(out, ref, what="bad pages")
+    assert PA.device_status(clear=True) & _native.NXT_PA_DEV_BAD_PAGE
+
+
+@pytest.mark.parametrize("name,fmt,fmax", FMTS)
+@pytest.mark.parametrize("head_size", [128, 40])
+def test_fp8_append_bit_exact(cuda, name, fmt, fmax, head_size):
+    import torch
+    rng = np.random.default_rng(head_size)
+    T, Hkv, nb, bs = 37, 4, 16, 16
+    key = (rng.standard_normal((T, Hkv, head_size)) * 3).astype(np.float16)
+    value = (rng.standard_normal((T, Hkv, head_size)) * 0.2).astype(np.float16)
+    key[0, 0, :4] = np.array([60000, -60000, 0, -0.0], dtype=np.float16)  # saturation, zeros
+    slots = rng.permutation(nb * bs)[:T].astype(np.int64)
+    slots[5] = -1  # skipped
+    ks, vs = 0.05, 0.001
+    kc = np.zeros((nb, Hkv, bs, head_size), dtype=np.uint8)
+    vc = np.zeros_like(kc)
+    kcd, vcd = torch.from_numpy(kc).to(cuda), torch.from_numpy(vc).to(cuda)
+    PA.reshape_and_cache_fp8(torch.from_numpy(key).to(cuda), torch.from_numpy(value).to(cuda),
+                             kcd, vcd, torch.from_numpy(slots).to(cuda), name, ks, vs)
+    torch.cuda.synchronize()
+    k8 = O.fp8_encode(key.astype(np.float32) / np.float32(ks), fmt)
+    v8 = O.fp8_encode(value.astype(np.float32) / np.float32(vs), fmt)
+    O.reshape_and_cache(k8, v8, kc, vc, slots, block_size=bs)
+    assert np.array_equal(kcd.cpu().numpy(), kc)
+    assert np.array_equal(vcd.cpu().numpy(), vc)

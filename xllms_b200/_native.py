@@ -29,6 +29,15 @@ NXT_PA_DEV_SEQ_CLAMPED = 0x4
 NXT_PA_PATH_NONE = 0
 NXT_PA_PATH_TMA_MMA = 1
 NXT_PA_PATH_GENERIC = 2
+NXT_BT_TABLES = 0
+NXT_BT_SEQ_LENS = 1
+NXT_BT_SLOTS = 2
+NXT_BT_PREFIX_PAGES = 3
+NXT_BT_GROUP_OFFSETS = 4
+NXT_BT_GROUP_MEMBERS = 5
+NXT_BT_NUM_ARRAYS = 6
+NXT_KV_FP8_E4M3 = 1
+NXT_KV_FP8_E5M2 = 2
 NXT_ACT_SILU_AND_MUL = 0
 NXT_ACT_MUL_AND_SILU = 1
 NXT_ACT_GELU_AND_MUL = 2
@@ -63,6 +72,10 @@ SIGNATURES = {
          _VP, _VP],
     ),
     "nxt_paged_attention_profile_next": (_I, [_VP, _VP]),
+    "nxt_block_tables_layout": (_SZ, [_I, _I, _I, _VP]),
+    "nxt_block_tables_staging_size": (_SZ, [_I, _I]),
+    "nxt_build_block_tables": (
+        _I, [_IP, _IP, _IP, _IP, _IP, _I, _I, _I, _VP, _SZ, _VP, _SZ, _IP, _IP, _IP, _VP]),
     "nxt_silu_and_mul": (None, [_VP, _CVP, _I, _I, _I, _VP]),
     "nxt_mul_and_silu": (None, [_VP, _CVP, _I, _I, _I, _VP]),
     "nxt_gelu_and_mul": (None, [_VP, _CVP, _I, _I, _I, _VP]),
@@ -77,6 +90,12 @@ SIGNATURES = {
          _I, _I64, _I64, _I64, _VP, _SZ, _VP, _VP],
     ),
     "nxt_paged_attention_prefix_workspace_size": (_SZ, [_I, _I, _I, _I, _I, _I, _I]),
+    "nxt_paged_attention_fp8_ex": (
+        _I,
+        [_VP, _CVP, _CVP, _CVP, _IP, _IP, _I, _I, _I, _I, _F, _I, _I, _I, _F, _F, _I64, _I64,
+         _I64, _VP, _SZ, _VP, _VP]),
+    "nxt_reshape_and_cache_fp8": (
+        _I, [_CVP, _CVP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _F, _I64, _I64, _I64, _VP]),
     "nxt_reshape_and_cache": (
         _I, [_CVP, _CVP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I64, _I64, _I64, _VP]),
     "nxt_paged_attention_append_ex": (

@@ -142,24 +142,28 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 64 x 16 x 1 x 1 with 128-byte swizzle. An unknown pool size uses the
 // largest page coordinate TMA accepts.
 bool encode_pool(CUtensorMap* m, const void* base, int D, int Hkv, long long num_blocks,
-                 long long kbs, long long khs) {
+                 long long kbs, long long khs, int es) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[4] = {(cuuint64_t)D, 16u, (cuuint64_t)Hkv,
                         (cuuint64_t)(num_blocks > 0 ? num_blocks : (long long)INT_MAX)};
-  cuuint64_t strides[3] = {(cuuint64_t)D * 2u, (cuuint64_t)khs * 2u, (cuuint64_t)kbs * 2u};
-  cuuint32_t box[4] = {64u, 16u, 1u, 1u};
+  cuuint64_t strides[3] = {(cuuint64_t)D * es, (cuuint64_t)khs * es, (cuuint64_t)kbs * es};
+  // one box row = 128 bytes (64 fp16 or 128 fp8 elements), the 128-byte swizzle span
+  cuuint32_t box[4] = {(cuuint32_t)(128 / es), 16u, 1u, 1u};
   cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides,
+  const CUtensorMapDataType dt =
+      es == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(m, dt, 4, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-bool fast_layout_ok(const void* k, const void* v, int D, int Hkv, long long kbs, long long khs) {
+bool fast_layout_ok(const void* k, const void* v, int D, int Hkv, long long kbs, long long khs,
+                    int es) {
   const uintptr_t a = reinterpret_cast<uintptr_t>(k), b = reinterpret_cast<uintptr_t>(v);
   if ((a | b) & 15u) return false;
-  if ((kbs * 2) % 16 || (khs * 2) % 16) return false;
+  if ((kbs * es) % 16 || (khs * es) % 16) return false;
   if (khs < 16LL * D) return false;             // a page's slots are contiguous rows
   if (Hkv > 1 && kbs < khs * Hkv && khs != 0) {
     // Non-standard order (heads outermost): tensor-map strides may then not
@@ -226,11 +230,18 @@ int prefix_chunk_pages(int max_prefix_pages) {
   return cp;
 }
 
+// Quantised KV cache of an fp8 call.
+struct KvQuant {
+  int fmt;  // xpa::kKvE4M3 or xpa::kKvE5M2
+  float k_scale, v_scale;
+};
+
 int run(void* out, const void* q, const void* k, const void* v, const int* bt, const int* sl,
         int B, int Hq, int D, int Hkv, float scale, int max_blocks, int bs, int ds,
         long long kbs, long long khs, long long num_blocks, void* ws, size_t ws_bytes,
         int* dev_status, cudaStream_t st, const NxtPaShard* shard = nullptr,
-        uint64_t step = 0, bool after_append = false, const PrefixArgs* pre = nullptr) {
+        uint64_t step = 0, bool after_append = false, const PrefixArgs* pre = nullptr,
+        const KvQuant* kvq = nullptr) {
   if (shard) {
     if (shard->world_size < 1 || shard->world_size > NXT_PA_MAX_PEERS || shard->rank < 0 ||
         shard->rank >= shard->world_size || step == 0 || shard->head_offset < 0 ||
@@ -242,6 +253,15 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   }
   int rc = check_args(out, q, k, v, bt, sl, B, Hq, D, Hkv, max_blocks, bs, ds, kbs, khs);
   if (rc != NXT_PA_OK || B == 0) return rc;
+  const int kv_fmt = kvq ? kvq->fmt : 0;
+  const int kv_es = kvq ? 1 : ds;
+  if (kvq) {
+    if ((kvq->fmt != xpa::kKvE4M3 && kvq->fmt != xpa::kKvE5M2) || ds != 2 ||
+        !(kvq->k_scale > 0.f) || !(kvq->v_scale > 0.f) || !std::isfinite(kvq->k_scale) ||
+        !std::isfinite(kvq->v_scale))
+      return NXT_PA_EINVAL;
+    pre = nullptr;  // the shared-prefix kernels read fp16 caches only
+  }
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NXT_PA_ECUDA;
@@ -249,11 +269,11 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   // A cascade call needs the TMA path's shapes; others run without the prefix
   // information, which gives the same result.
   CUtensorMap tk, tv;
-  const bool fast = xpa::fast_path_shape_ok(D, Hq / Hkv, bs, ds) &&
-                    fast_layout_ok(k, v, D, Hkv, kbs, khs) &&
-                    (reinterpret_cast<uintptr_t>(q) & 3u) == 0 &&
-                    encode_pool(&tk, k, D, Hkv, num_blocks, kbs, khs) &&
-                    encode_pool(&tv, v, D, Hkv, num_blocks, kbs, khs);
+  const bool fast = xpa::fast_path_shape_ok(D, Hq / Hkv, bs, ds, kv_fmt) &&
+                    fast_layout_ok(k, v, D, Hkv, kbs, khs, kv_es) &&
+                    (reinterpret_cast<uintptr_t>(q) & (kv_fmt ? 7u : 3u)) == 0 &&
+                    encode_pool(&tk, k, D, Hkv, num_blocks, kbs, khs, kv_es) &&
+                    encode_pool(&tv, v, D, Hkv, num_blocks, kbs, khs, kv_es);
   if (pre && (!fast || pre->num_groups <= 0 || pre->max_prefix_pages <= 0 ||
               pre->max_group_size <= 0))
     pre = nullptr;
@@ -321,7 +341,9 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   p.slots = slots;
   p.prefix_pages = pre ? pre->prefix_pages : nullptr;
   p.prefix_chunk = pchunk;
-  p.scale_log2 = scale * 1.4426950408889634f;
+  p.scale_log2 = scale * (kvq ? kvq->k_scale : 1.f) * 1.4426950408889634f;
+  p.kv_fmt = kv_fmt;
+  p.v_scale = kvq ? kvq->v_scale : 1.f;
   p.after_append = after_append ? 1 : 0;
   {
     auto a16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
@@ -564,6 +586,62 @@ size_t nxt_paged_attention_prefix_workspace_size(int num_seqs, int num_heads, in
       max_prefix_pages > 0 ? ceil_div(max_prefix_pages, prefix_chunk_pages(max_prefix_pages)) : 0;
   return (size_t)num_seqs * num_heads * (pl.max_parts + pchunks) * (size_t)(head_size + 2) *
          sizeof(float);
+}
+
+int nxt_paged_attention_fp8_ex(void* out, const void* query, const void* key_cache,
+                               const void* value_cache, const int* block_tables,
+                               const int* seq_lens, int num_seqs, int num_heads, int head_size,
+                               int num_kv_heads, float scale, int max_num_blocks_per_seq,
+                               int block_size, int kv_format, float k_scale, float v_scale,
+                               int64_t kv_block_stride, int64_t kv_head_stride,
+                               int64_t num_blocks, void* workspace, size_t workspace_bytes,
+                               int* device_status, nxt_stream_t stream) {
+  const KvQuant kq{kv_format, k_scale, v_scale};
+  return run(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads,
+             head_size, num_kv_heads, scale, max_num_blocks_per_seq, block_size, 2,
+             kv_block_stride, kv_head_stride, num_blocks, workspace, workspace_bytes,
+             device_status, static_cast<cudaStream_t>(stream), nullptr, 0, false, nullptr, &kq);
+}
+
+int nxt_reshape_and_cache_fp8(const void* key, const void* value, void* key_cache,
+                              void* value_cache, const int64_t* slot_mapping, int num_tokens,
+                              int num_kv_heads, int head_size, int block_size, int kv_format,
+                              float k_scale, float v_scale, int64_t kv_block_stride,
+                              int64_t kv_head_stride, int64_t token_stride, nxt_stream_t stream) {
+  if (num_tokens < 0) return NXT_PA_EINVAL;
+  if (num_tokens == 0) return NXT_PA_OK;
+  if (!key || !value || !key_cache || !value_cache || !slot_mapping) return NXT_PA_EINVAL;
+  if ((kv_format != xpa::kKvE4M3 && kv_format != xpa::kKvE5M2) || !(k_scale > 0.f) ||
+      !(v_scale > 0.f) || !std::isfinite(k_scale) || !std::isfinite(v_scale))
+    return NXT_PA_EINVAL;
+  if (num_kv_heads <= 0 || head_size <= 0 || head_size > 256 || block_size <= 0 ||
+      kv_block_stride < 0 || kv_head_stride < 0 ||
+      token_stride < (int64_t)num_kv_heads * head_size)
+    return NXT_PA_EINVAL;
+  xpa::AppendParams a{};
+  a.key = key;
+  a.value = value;
+  a.key_cache = key_cache;
+  a.value_cache = value_cache;
+  a.slots = reinterpret_cast<const long long*>(slot_mapping);
+  a.kv_block_stride = kv_block_stride;
+  a.kv_head_stride = kv_head_stride;
+  a.token_stride = token_stride;
+  a.num_tokens = num_tokens;
+  a.Hkv = num_kv_heads;
+  a.D = head_size;
+  a.block_size = block_size;
+  a.kv_fmt = kv_format;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  auto al = [](const void* x, unsigned m) { return (reinterpret_cast<uintptr_t>(x) & m) == 0; };
+  // 8 fp16 in (16 bytes), 8 fp8 out (8 bytes) per lane step
+  a.vec16 = (head_size % 8 == 0 && kv_block_stride % 8 == 0 && kv_head_stride % 8 == 0 &&
+             (token_stride * 2) % 16 == 0 && al(key, 15u) && al(value, 15u) &&
+             al(key_cache, 7u) && al(value_cache, 7u))
+                ? 1
+                : 0;
+  return map_cuda(xpa::launch_append(a, 2, static_cast<cudaStream_t>(stream)));
 }
 
 int nxt_reshape_and_cache(const void* key, const void* value, void* key_cache, void* value_cache,

@@ -55,7 +55,15 @@ struct Params {
   // griddepcontrol.wait (the appended token lives there).
   int after_append;
   int join_primary;  // CTA 0 waits for the preceding grid before it exits
+  // Quantised KV cache: 0 = K/V in the query's dtype; kKvE4M3 / kKvE5M2 = one
+  // fp8 byte per element holding encode(x / scale). k_scale is folded into
+  // scale_log2; v_scale multiplies V (generic path) or O (fast path).
+  int kv_fmt;
+  float v_scale;
 };
+
+constexpr int kKvE4M3 = 1;
+constexpr int kKvE5M2 = 2;
 
 // KV append: token t's rows key/value[t*token_stride + h*D + d] go to the
 // pool slot slots[t] (page slot/block_size, slot slot%block_size).
@@ -68,6 +76,11 @@ struct AppendParams {
   long long kv_block_stride, kv_head_stride, token_stride;
   int num_tokens, Hkv, D, block_size;
   int vec16;  // every row 16-byte aligned: copy 16 bytes per lane
+  // fp8 cache (kKvE4M3 / kKvE5M2): the fp16 rows are stored as
+  // encode(x / k_scale) and encode(x / v_scale), rounded to nearest even and
+  // saturated at the format's largest finite value. 0: bit copy.
+  int kv_fmt;
+  float k_scale, v_scale;
 };
 
 // One unit of work: context partition `part` of (sequence b, KV head kvh).
@@ -284,6 +297,36 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
   return y;
+}
+
+// Two fp8 values (low byte first) -> fp16x2 (low half first); exact, since
+// every E4M3 and E5M2 value is an fp16 value.
+template <int FMT>
+__device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t two) {
+  uint32_t r;
+  const unsigned short v = (unsigned short)(two & 0xffffu);
+  if constexpr (FMT == kKvE4M3)
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(v));
+  else
+    asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(r) : "h"(v));
+  return r;
+}
+template <int FMT>
+__device__ __forceinline__ float fp8_to_float(uint8_t b) {
+  const uint32_t h2 = fp8x2_to_h2<FMT>(b);
+  return __half2float(__ushort_as_half((unsigned short)(h2 & 0xffffu)));
+}
+// (a, b) -> two fp8 bytes, a in the low byte; round to nearest even,
+// saturating at the largest finite value (NaN stays NaN).
+template <int FMT>
+__device__ __forceinline__ uint32_t float2_to_fp8x2(float a, float b) {
+  unsigned short r;
+  // the first source operand lands in the upper byte
+  if constexpr (FMT == kKvE4M3)
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  else
+    asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  return r;
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {

@@ -21,12 +21,14 @@ struct Plan {
 };
 Plan make_plan(int B, int Hq, int D, int Hkv, int max_blocks, int nsm);
 
-// Tensor map of one fp16 pool for the TMA path; false when it cannot be encoded.
+// Tensor map of one pool for the TMA path; false when it cannot be encoded.
+// es: bytes per K / V element (2 = fp16, 1 = fp8).
 bool encode_pool(CUtensorMap* m, const void* base, int D, int Hkv, long long num_blocks,
-                 long long kbs, long long khs);
+                 long long kbs, long long khs, int es = 2);
 
 // Pool alignment and stride order the TMA path needs.
-bool fast_layout_ok(const void* k, const void* v, int D, int Hkv, long long kbs, long long khs);
+bool fast_layout_ok(const void* k, const void* v, int D, int Hkv, long long kbs, long long khs,
+                    int es = 2);
 
 // NXT_PA_OK or NXT_PA_EINVAL for the argument set of one call.
 int check_args(const void* out, const void* q, const void* k, const void* v, const int* bt,

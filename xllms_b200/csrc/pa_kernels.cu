@@ -29,7 +29,16 @@ namespace xpa {
 // dimension (DPL dims per lane) and each token's K row is used for HG query
 // heads of the group at once, so K/V are read once per HG heads.
 // ════════════════════════════════════════════════════════════════════════
-template <typename T, int DPL, int HG>
+// K/V element idx of a pool: T, or an fp8 byte (KVF = kKvE4M3 / kKvE5M2).
+template <typename T, int KVF>
+__device__ __forceinline__ float kv_load(const void* base, long long idx) {
+  if constexpr (KVF == 0)
+    return to_float(static_cast<const T*>(base)[idx]);
+  else
+    return fp8_to_float<KVF>(static_cast<const uint8_t*>(base)[idx]);
+}
+
+template <typename T, int DPL, int HG, int KVF>
 __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
   constexpr int NW = 4;
   constexpr int DMAX = DPL * 32;
@@ -51,8 +60,7 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   if (p.after_append) pdl_wait_primary();  // appended tokens are read like any other
   const T* Q = static_cast<const T*>(p.q);
-  const T* K = static_cast<const T*>(p.k);
-  const T* V = static_cast<const T*>(p.v);
+  const float vs = KVF ? p.v_scale : 1.f;  // k_scale is in scale_log2
   const int* bt_row = p.block_tables + (long long)it.b * p.max_blocks;
   const int t_begin = it.page_begin * p.block_size;
   const int t_end = min(it.L, it.page_end * p.block_size);
@@ -86,8 +94,8 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
 #pragma unroll
       for (int i = 0; i < DPL; ++i) {
         const int d = lane + 32 * i;
-        kf[i] = d < D ? to_float(K[base + d]) : 0.f;
-        vf[i] = d < D ? to_float(V[base + d]) : 0.f;
+        kf[i] = d < D ? kv_load<T, KVF>(p.k, base + d) : 0.f;
+        vf[i] = d < D ? kv_load<T, KVF>(p.v, base + d) * vs : 0.f;
       }
 #pragma unroll
       for (int j = 0; j < HG; ++j) {
@@ -163,23 +171,27 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
 // Bound on the producer's wait for its own in-flight copies after a timeout.
 constexpr uint64_t kDrainBudgetNs = 1000000000ull;
 
-template <int D, int NT, int STAGES, int NWC>
+template <int D, int NT, int STAGES, int NWC, int KVF>
 struct FastCfg {
-  static constexpr int kTile = 16 * D * 2;     // bytes of one K (or V) page
-  static constexpr int kStage = 2 * kTile;     // K + V
+  static constexpr int kElem = KVF ? 1 : 2;      // bytes per K / V element
+  static constexpr int kTile = 16 * D * kElem;   // bytes of one K (or V) page
+  static constexpr int kStage = 2 * kTile;       // K + V
   static constexpr int kKSteps = D / 16;
-  static constexpr int kBoxes = D / 64;
+  static constexpr int kBoxes = D * kElem / 128; // 128-byte-wide TMA boxes per row
+  static constexpr int kBoxElems = 128 / kElem;
   static constexpr int kRing = STAGES * kStage;
+  // fp8 caches: each consumer warp widens its V page to an fp16 tile here
+  static constexpr int kV16 = KVF ? NWC * 16 * D * 2 : 0;
   static constexpr int kMerge = NWC * NT * 8 * (D + 4) * 4 + NWC * NT * 8 * 8;
-  static constexpr int kBarOff = kRing > kMerge ? kRing : kMerge;
+  static constexpr int kBarOff = kRing + kV16 > kMerge ? kRing + kV16 : kMerge;
   static constexpr int kSmem = 1024 + kBarOff + STAGES * 16 + STAGES * 4;
   static constexpr int kThreads = (NWC + 1) * 32;
 };
 
-template <int D, int NT, int STAGES, int NWC>
+template <int D, int NT, int STAGES, int NWC, int KVF>
 __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUtensorMap& tmV,
                                              const Params& p) {
-  using C = FastCfg<D, NT, STAGES, NWC>;
+  using C = FastCfg<D, NT, STAGES, NWC, KVF>;
   // Page j goes to stage j % STAGES and to consumer warp j % NWC. The parity
   // waits below are only sound when every stage always belongs to the same
   // warp: otherwise a warp could test a stage one phase early, see the parity
@@ -251,8 +263,8 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
             const uint32_t tk = sbase + s * C::kStage, tv = tk + C::kTile;
 #pragma unroll
             for (int x = 0; x < C::kBoxes; ++x) {
-              tma_load_4d(tk + x * 2048, &tmK, x * 64, 0, it.kvh, phys, full);
-              tma_load_4d(tv + x * 2048, &tmV, x * 64, 0, it.kvh, phys, full);
+              tma_load_4d(tk + x * 2048, &tmK, x * C::kBoxElems, 0, it.kvh, phys, full);
+              tma_load_4d(tv + x * 2048, &tmV, x * C::kBoxElems, 0, it.kvh, phys, full);
             }
           } else {
             raise_status(p, kDevBadPage);
@@ -278,14 +290,22 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
   const __half* qrow =
       static_cast<const __half*>(p.q) + ((long long)it.b * p.Hq + (long long)it.kvh * GS) * D;
   // Q^T as the B operand (k = d, n = head): lane (g, c) holds
-  // Q[head g][16ks + 2c, +1] and Q[head g][16ks + 8 + 2c, +1].
+  // Q[head g][16ks + 2c, +1] and Q[head g][16ks + 8 + 2c, +1]. With an fp8
+  // cache the k index of a step is permuted, the same way for K and Q, so
+  // that lane c's four K elements are four consecutive bytes: k (2c, 2c+1,
+  // 2c+8, 2c+9) <-> d 16ks + 4c + (0, 1, 2, 3).
   uint32_t qf[NT][C::kKSteps][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int head = nt * 8 + g;
 #pragma unroll
     for (int ks = 0; ks < C::kKSteps; ++ks) {
-      if (head < GS) {
+      if (head < GS && KVF) {
+        const uint2 q4 =
+            __ldg(reinterpret_cast<const uint2*>(qrow + head * D + ks * 16 + 4 * c));
+        qf[nt][ks][0] = q4.x;
+        qf[nt][ks][1] = q4.y;
+      } else if (head < GS) {
         const __half* qp = qrow + head * D + ks * 16 + 2 * c;
         qf[nt][ks][0] = __ldg(reinterpret_cast<const unsigned int*>(qp));
         qf[nt][ks][1] = __ldg(reinterpret_cast<const unsigned int*>(qp + 8));
@@ -329,13 +349,58 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
 #pragma unroll
       for (int ks = 0; ks < C::kKSteps; ++ks) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4(tk + tile_off(r8 + ((mi & 1) << 3), 2 * ks + (mi >> 1)), a0, a1, a2, a3);
+        if constexpr (KVF != 0) {
+          // fp8 rows of 128 bytes, 16-byte chunk ks % 8 of box ks / 8 (chunk
+          // index XOR row % 8); lane (g, c) reads 4 bytes of tokens g, g + 8
+          const uint32_t off = (uint32_t)((ks >> 3) * 2048 + (((ks & 7) ^ g) << 4) + 4 * c);
+          uint32_t w0, w1;
+          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w0) : "r"(tk + off + g * 128));
+          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w1) : "r"(tk + off + (g + 8) * 128));
+          a0 = fp8x2_to_h2<KVF>(w0);
+          a2 = fp8x2_to_h2<KVF>(w0 >> 16);
+          a1 = fp8x2_to_h2<KVF>(w1);
+          a3 = fp8x2_to_h2<KVF>(w1 >> 16);
+        } else {
+          ldsm_x4(tk + tile_off(r8 + ((mi & 1) << 3), 2 * ks + (mi >> 1)), a0, a1, a2, a3);
+        }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
           mma_f16_16816(sc[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
       }
 
-      if (ntok < 16) {
+      // fp8 cache: widen the V page into this warp's fp16 tile (rows >=
+      // ntok as zeros), in the fp16 tile layout the PV loads below expect;
+      // the ring stage is then free for the producer.
+      uint32_t vsrc = tv;
+      if constexpr (KVF != 0) {
+        vsrc = sbase + C::kRing + warp * (16 * D * 2);
+        constexpr int CH8 = D / 16;  // 16-byte fp8 chunks per row
+        // lanes of one 8-lane store phase take 8 rows of one chunk column:
+        // distinct swizzled 16-byte slots, no bank conflicts
+        for (int qi = lane; qi < 16 * CH8; qi += 32) {
+          const int row = qi & 15, c8 = qi >> 4;
+          uint4 w = make_uint4(0u, 0u, 0u, 0u);
+          if (row < ntok)
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                         : "r"(tv + (c8 >> 3) * 2048 + row * 128 + (((c8 & 7) ^ (row & 7)) << 4)));
+          const uint32_t h0 = fp8x2_to_h2<KVF>(w.x), h1 = fp8x2_to_h2<KVF>(w.x >> 16);
+          const uint32_t h2 = fp8x2_to_h2<KVF>(w.y), h3 = fp8x2_to_h2<KVF>(w.y >> 16);
+          const uint32_t h4 = fp8x2_to_h2<KVF>(w.z), h5 = fp8x2_to_h2<KVF>(w.z >> 16);
+          const uint32_t h6 = fp8x2_to_h2<KVF>(w.w), h7 = fp8x2_to_h2<KVF>(w.w >> 16);
+          const int chunk = 2 * c8;  // 8-element fp16 chunk of d = 16 c8
+          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(vsrc + tile_off(row, chunk)),
+                       "r"(h0), "r"(h1), "r"(h2), "r"(h3)
+                       : "memory");
+          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(vsrc + tile_off(row, chunk + 1)),
+                       "r"(h4), "r"(h5), "r"(h6), "r"(h7)
+                       : "memory");
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_empty + 8 * s);
+      }
+
+      if (KVF == 0 && ntok < 16) {
         // Last page of the sequence: slots >= ntok hold whatever the pool
         // holds; clear them in V so 0 * (inf or NaN) cannot enter PV.
         const int nclr = (16 - ntok) * C::kBoxes * 8;
@@ -394,17 +459,20 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
 #pragma unroll
       for (int mt = 0; mt < C::kKSteps; ++mt) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4_trans(tv + tile_off(r8 + ((mi >> 1) << 3), 2 * mt + (mi & 1)), a0, a1, a2, a3);
+        ldsm_x4_trans(vsrc + tile_off(r8 + ((mi >> 1) << 3), 2 * mt + (mi & 1)), a0, a1, a2, a3);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           mma_f16_16816(o[nt][mt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
           mma_f16_16816(o[nt][mt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
         }
       }
-      if (ntok < 16) fence_proxy_async_smem();
+      if (KVF == 0 && ntok < 16) fence_proxy_async_smem();
+      __syncwarp();  // this warp's fp16 V tile is rewritten for its next page
+      if (KVF == 0 && lane == 0) mbar_arrive(bar_empty + 8 * s);
+    } else {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_empty + 8 * s);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar_empty + 8 * s);
   }
 
   // ── merge the consumer warps' states ─────────────────────────────────
@@ -469,6 +537,10 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
         num[7] = fmaf(wt, b.w, num[7]);
       }
     }
+    if constexpr (KVF != 0) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) num[k] *= p.v_scale;
+    }
     if (it.direct) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) num[k] = den > 0.f ? num[k] / den : 0.f;
@@ -491,11 +563,14 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
   }
 }
 
-template <int D, int NT, int STAGES, int NWC>
-__global__ void __launch_bounds__((NWC + 1) * 32)
+#ifndef XPA_FP8_MIN_CTAS
+#define XPA_FP8_MIN_CTAS 1
+#endif
+template <int D, int NT, int STAGES, int NWC, int KVF>
+__global__ void __launch_bounds__((NWC + 1) * 32, KVF ? XPA_FP8_MIN_CTAS : 1)
     pa_tma_mma_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const Params p) {
-  tma_mma_body<D, NT, STAGES, NWC>(tmK, tmV, p);
+  tma_mma_body<D, NT, STAGES, NWC, KVF>(tmK, tmV, p);
   // Beside a running shared-prefix grid: this grid may not complete before
   // that one has (the merge after it reads both grids' partials).
   if (p.join_primary && blockIdx.x == 0) pdl_wait_primary();
@@ -609,6 +684,49 @@ __global__ void __launch_bounds__(128) pa_append_kernel(AppendParams a) {
   }
 }
 
+// KV append into an fp8 cache: fp16 rows in, encode(x / scale) bytes out
+// (round to nearest even, saturating), 8 elements per lane and step when
+// every row is 16-byte (source) / 8-byte (cache) aligned.
+template <int KVF>
+__global__ void __launch_bounds__(128) pa_append_fp8_kernel(AppendParams a) {
+  pdl_launch_dependents();
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long long)a.num_tokens * a.Hkv) return;
+  const int t = (int)(w / a.Hkv), h = (int)(w % a.Hkv);
+  const long long slot = a.slots[t];
+  if (slot < 0) return;
+  const long long page = slot / a.block_size, s = slot % a.block_size;
+  const long long dst = page * a.kv_block_stride + (long long)h * a.kv_head_stride + s * a.D;
+  const long long src = (long long)t * a.token_stride + (long long)h * a.D;
+  const __half* k = static_cast<const __half*>(a.key) + src;
+  const __half* v = static_cast<const __half*>(a.value) + src;
+  uint8_t* kc = static_cast<uint8_t*>(a.key_cache) + dst;
+  uint8_t* vc = static_cast<uint8_t*>(a.value_cache) + dst;
+  const float ks = a.k_scale, vs = a.v_scale;
+  auto q8 = [&](uint4 x, float sc) {  // 8 fp16 -> 8 fp8 bytes
+    const __half2* h2 = reinterpret_cast<const __half2*>(&x);
+    uint32_t b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h2[i]);
+      b[i] = float2_to_fp8x2<KVF>(f.x / sc, f.y / sc);
+    }
+    return make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
+  };
+  if (a.vec16) {
+    for (int i = lane; i < a.D / 8; i += 32) {
+      reinterpret_cast<uint2*>(kc)[i] = q8(__ldg(reinterpret_cast<const uint4*>(k) + i), ks);
+      reinterpret_cast<uint2*>(vc)[i] = q8(__ldg(reinterpret_cast<const uint4*>(v) + i), vs);
+    }
+  } else {
+    for (int i = lane; i < a.D; i += 32) {
+      kc[i] = (uint8_t)(float2_to_fp8x2<KVF>(__half2float(k[i]) / ks, 0.f) & 0xffu);
+      vc[i] = (uint8_t)(float2_to_fp8x2<KVF>(__half2float(v[i]) / vs, 0.f) & 0xffu);
+    }
+  }
+}
+
 // ════════════════════════════════════════════════════════════════════════
 // Launchers
 // ════════════════════════════════════════════════════════════════════════
@@ -635,8 +753,14 @@ cudaError_t launch_ex(void (*kern)(KArgs...), unsigned grid, unsigned block, siz
 template <typename T, int DPL, int HG>
 cudaError_t launch_generic_t(const Params& p, cudaStream_t st) {
   const long long grid = (long long)p.B * p.Hkv * p.max_parts;
-  return launch_ex(pa_generic_kernel<T, DPL, HG>, (unsigned)grid, 128, 0, st,
-                   p.after_append != 0, p);
+  const bool pdl = p.after_append != 0;
+  if constexpr (sizeof(T) == 2) {  // fp8 caches pair with fp16 queries
+    if (p.kv_fmt == kKvE4M3)
+      return launch_ex(pa_generic_kernel<T, DPL, HG, kKvE4M3>, (unsigned)grid, 128, 0, st, pdl, p);
+    if (p.kv_fmt == kKvE5M2)
+      return launch_ex(pa_generic_kernel<T, DPL, HG, kKvE5M2>, (unsigned)grid, 128, 0, st, pdl, p);
+  }
+  return launch_ex(pa_generic_kernel<T, DPL, HG, 0>, (unsigned)grid, 128, 0, st, pdl, p);
 }
 
 template <typename T, int DPL>
@@ -675,22 +799,35 @@ cudaError_t launch_generic_typed(const Params& p, cudaStream_t st) {
 #define XPA_CONSUMER_WARPS 2
 #endif
 
-template <int D, int NT>
+template <int D, int NT, int KVF>
 cudaError_t launch_fast_t(const CUtensorMap& tk, const CUtensorMap& tv, const Params& p,
                           cudaStream_t st) {
   constexpr int STAGES = (D == 256) ? (XPA_RING_PAGES / 2 > 1 ? XPA_RING_PAGES / 2 : 2)
                                     : XPA_RING_PAGES;
   constexpr int NWC = XPA_CONSUMER_WARPS;
-  using C = FastCfg<D, NT, STAGES, NWC>;
-  auto kern = pa_tma_mma_kernel<D, NT, STAGES, NWC>;
+  using C = FastCfg<D, NT, STAGES, NWC, KVF>;
+  auto kern = pa_tma_mma_kernel<D, NT, STAGES, NWC, KVF>;
   // The attribute is per function and device; setting it every call costs
   // a driver call only.
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   if (e != cudaSuccess) return e;
+  // all of the SM's unified L1 / shared storage as shared memory: the
+  // resident-CTA count, not L1 hits, keeps the page stream going
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
   const long long grid = (long long)p.B * p.Hkv * p.max_parts;
   return launch_ex(kern, (unsigned)grid, C::kThreads, C::kSmem, st,
                    p.after_append != 0 || p.join_primary != 0, tk, tv, p);
+}
+
+template <int D, int NT>
+cudaError_t launch_fast_kv(const CUtensorMap& tk, const CUtensorMap& tv, const Params& p,
+                           cudaStream_t st) {
+  if (p.kv_fmt == kKvE4M3) return launch_fast_t<D, NT, kKvE4M3>(tk, tv, p, st);
+  if (p.kv_fmt == kKvE5M2) return launch_fast_t<D, NT, kKvE5M2>(tk, tv, p, st);
+  return launch_fast_t<D, NT, 0>(tk, tv, p, st);
 }
 
 }  // namespace
@@ -700,9 +837,10 @@ cudaError_t launch_generic(const Params& p, int dtype_size, cudaStream_t st) {
                          : launch_generic_typed<__half>(p, st);
 }
 
-bool fast_path_shape_ok(int head_size, int group, int block_size, int dtype_size) {
+bool fast_path_shape_ok(int head_size, int group, int block_size, int dtype_size, int kv_fmt) {
   if (dtype_size != 2 || block_size != 16) return false;
   if (head_size != 64 && head_size != 128 && head_size != 256) return false;
+  if (kv_fmt != 0 && head_size == 64) return false;  // fp8 rows narrower than a 128-byte box
   if (group < 1 || group > 16) return false;
   if (group > 8 && head_size == 256) return false;  // accumulator registers
   return true;
@@ -712,9 +850,12 @@ cudaError_t launch_fast(const CUtensorMap& tk, const CUtensorMap& tv, const Para
                         cudaStream_t st) {
   const bool two = p.GS > 8;
   switch (p.D) {
-    case 64: return two ? launch_fast_t<64, 2>(tk, tv, p, st) : launch_fast_t<64, 1>(tk, tv, p, st);
-    case 128: return two ? launch_fast_t<128, 2>(tk, tv, p, st) : launch_fast_t<128, 1>(tk, tv, p, st);
-    case 256: return launch_fast_t<256, 1>(tk, tv, p, st);
+    case 64:
+      if (p.kv_fmt) return cudaErrorInvalidValue;
+      return two ? launch_fast_t<64, 2, 0>(tk, tv, p, st) : launch_fast_t<64, 1, 0>(tk, tv, p, st);
+    case 128:
+      return two ? launch_fast_kv<128, 2>(tk, tv, p, st) : launch_fast_kv<128, 1>(tk, tv, p, st);
+    case 256: return launch_fast_kv<256, 1>(tk, tv, p, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -739,7 +880,11 @@ cudaError_t launch_append(const AppendParams& a, int dtype_size, cudaStream_t st
   const long long warps = (long long)a.num_tokens * a.Hkv;
   const unsigned grid = (unsigned)((warps * 32 + 127) / 128);
   if (grid == 0) return cudaSuccess;
-  if (dtype_size == 4)
+  if (a.kv_fmt == kKvE4M3)
+    pa_append_fp8_kernel<kKvE4M3><<<grid, 128, 0, st>>>(a);
+  else if (a.kv_fmt == kKvE5M2)
+    pa_append_fp8_kernel<kKvE5M2><<<grid, 128, 0, st>>>(a);
+  else if (dtype_size == 4)
     pa_append_kernel<float><<<grid, 128, 0, st>>>(a);
   else
     pa_append_kernel<__half><<<grid, 128, 0, st>>>(a);

@@ -308,11 +308,14 @@ class PrefixGroups:
     list of (member sequence ids, shared prefix pages) pairs."""
 
     def __init__(self, groups, num_seqs, device=None, *, prefix_pages=None, offsets=None,
-                 members=None):
+                 members=None, bounds=None):
         import torch
-        self.num_groups = len(groups)
-        self.max_group_size = max((len(m) for m, _ in groups), default=0)
-        self.max_prefix_pages = max((int(p) for _, p in groups), default=0)
+        if bounds is not None:  # (num_groups, max_group_size, max_prefix_pages)
+            self.num_groups, self.max_group_size, self.max_prefix_pages = (int(x) for x in bounds)
+        else:
+            self.num_groups = len(groups)
+            self.max_group_size = max((len(m) for m, _ in groups), default=0)
+            self.max_prefix_pages = max((int(p) for _, p in groups), default=0)
         if prefix_pages is None:
             pp, off, mem = self.host_arrays(groups, num_seqs)
             t = lambda x: torch.from_numpy(x).to(device)
@@ -400,3 +403,117 @@ def activation(name, x, *, out=None, stream=None):
     if rc != _native.NXT_PA_OK:
         raise PagedAttentionError(rc, "nxt_activation_ex")
     return out
+
+
+# ── fp8 KV cache ───────────────────────────────────────────────────────────
+FP8_FORMATS = {"e4m3": _native.NXT_KV_FP8_E4M3, "e5m2": _native.NXT_KV_FP8_E5M2}
+
+
+def _fp8_code(fmt):
+    return FP8_FORMATS[fmt] if isinstance(fmt, str) else int(fmt)
+
+
+def paged_attention_fp8(query, key_cache, value_cache, block_tables, seq_lens, fmt, k_scale,
+                        v_scale, *, scale=None, out=None, num_blocks=None, workspace=None,
+                        device_status=None, stream=None):
+    """Decode attention over fp8 pools (uint8 tensors [NB, Hkv, P, D] holding
+    encode(x / scale)); query and output fp16 [B, Hq, D]."""
+    import torch
+    B, Hq, D = query.shape
+    nb, Hkv, bs, _ = key_cache.shape
+    if key_cache.element_size() != 1 or value_cache.element_size() != 1:
+        raise PagedAttentionError(_native.NXT_PA_EINVAL, "fp8 pools must be 1-byte tensors")
+    if out is None:
+        out = torch.empty_like(query)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (_ptr(workspace),
+                                                            workspace.numel() * workspace.element_size())
+    rc = _native.xpa().nxt_paged_attention_fp8_ex(
+        _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+        _ptr(seq_lens), B, Hq, D, Hkv, float(scale), block_tables.shape[1], bs, _fp8_code(fmt),
+        float(k_scale), float(v_scale), Hkv * bs * D, bs * D,
+        nb if num_blocks is None else int(num_blocks), ws_ptr, ws_bytes, _ptr(device_status),
+        _stream_ptr(stream))
+    if rc != _native.NXT_PA_OK:
+        raise PagedAttentionError(rc, "nxt_paged_attention_fp8_ex")
+    return out
+
+
+def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, fmt, k_scale, v_scale,
+                          stream=None) -> None:
+    """Quantise fp16 key/value [T, Hkv, D] into the fp8 pools [NB, Hkv, P, D]
+    at slot_mapping[t] (int64; negative: skipped)."""
+    T, Hkv, D = key.shape
+    nb, hk, bs, dk = key_cache.shape
+    if (hk != Hkv or dk != D or tuple(value.shape) != tuple(key.shape)
+            or tuple(value_cache.shape) != tuple(key_cache.shape)
+            or key_cache.element_size() != 1 or value_cache.element_size() != 1
+            or not (key_cache.is_contiguous() and value_cache.is_contiguous())
+            or key.stride(1) != D or value.stride() != key.stride()
+            or slot_mapping.numel() < T):
+        raise PagedAttentionError(_native.NXT_PA_EINVAL, "reshape_and_cache_fp8: shapes")
+    rc = _native.xpa().nxt_reshape_and_cache_fp8(
+        _ptr(key), _ptr(value), _ptr(key_cache), _ptr(value_cache), _ptr(slot_mapping), T, Hkv, D,
+        bs, _fp8_code(fmt), float(k_scale), float(v_scale), Hkv * bs * D, bs * D, key.stride(0),
+        _stream_ptr(stream))
+    if rc != _native.NXT_PA_OK:
+        raise PagedAttentionError(rc, "nxt_reshape_and_cache_fp8")
+
+
+# ── block-table builder ────────────────────────────────────────────────────
+class BlockTables:
+    """One decode step's kernel inputs on the device, built by
+    nxt_build_block_tables: tables [B, max_blocks] int32, seq_lens [B],
+    slots [B] int64 (the newest token's slot), prefix (PrefixGroups or None)."""
+
+    def __init__(self, buffer, offsets, B, max_blocks, bounds):
+        import torch
+        self.buffer = buffer
+
+        def view(key, n, dtype):
+            o = offsets[key]
+            es = torch.tensor([], dtype=dtype).element_size()
+            return buffer[o:o + n * es].view(dtype)
+        self.tables = view(_native.NXT_BT_TABLES, B * max_blocks, torch.int32).view(B, max_blocks)
+        self.seq_lens = view(_native.NXT_BT_SEQ_LENS, B, torch.int32)
+        self.slots = view(_native.NXT_BT_SLOTS, B, torch.int64)
+        pp = view(_native.NXT_BT_PREFIX_PAGES, B, torch.int32)
+        go = view(_native.NXT_BT_GROUP_OFFSETS, B + 1, torch.int32)
+        mem = view(_native.NXT_BT_GROUP_MEMBERS, B, torch.int32)
+        self.prefix = (PrefixGroups(None, B, prefix_pages=pp, offsets=go, members=mem,
+                                    bounds=bounds) if bounds[0] > 0 else None)
+
+
+def build_block_tables(page_lists, seq_lens, max_blocks, *, block_size=16, prefix_node=None,
+                       prefix_pages=None, device=None, stream=None, staging=None):
+    """page_lists: per sequence, its physical pages in token order; seq_lens:
+    context tokens (newest included); prefix_node / prefix_pages: per
+    sequence, the radix node of its shared prefix (-1: none) and the whole
+    pages it covers. Returns BlockTables on `device`."""
+    import numpy as np
+    import torch
+    B = len(page_lists)
+    counts = np.array([len(p) for p in page_lists], dtype=np.int64)
+    offs = np.zeros(B + 1, dtype=np.int32)
+    np.cumsum(counts, out=offs[1:])
+    ids = (np.concatenate([np.asarray(p, dtype=np.int32) for p in page_lists])
+           if B and offs[-1] else np.zeros(1, dtype=np.int32))
+    sl = np.ascontiguousarray(seq_lens, dtype=np.int32)
+    node = None if prefix_node is None else np.ascontiguousarray(prefix_node, dtype=np.int32)
+    ppg = None if prefix_pages is None else np.ascontiguousarray(prefix_pages, dtype=np.int32)
+    lib = _native.xpa()
+    offsets = (ctypes.c_size_t * _native.NXT_BT_NUM_ARRAYS)()
+    total = lib.nxt_block_tables_layout(B, int(max_blocks), int(offs[-1]), offsets)
+    buf = torch.empty(max(total, 16), dtype=torch.uint8, device=device)
+    g = (ctypes.c_int * 3)()
+    ptr = lambda a: None if a is None else a.ctypes.data
+    st_ptr, st_bytes = (None, 0) if staging is None else (staging.data_ptr(),
+                                                          staging.numel() * staging.element_size())
+    rc = lib.nxt_build_block_tables(
+        ptr(offs), ptr(ids), ptr(sl), ptr(node), ptr(ppg), B, int(max_blocks), int(block_size),
+        _ptr(buf), total, st_ptr, st_bytes, ctypes.addressof(g),
+        ctypes.addressof(g) + 4, ctypes.addressof(g) + 8, _stream_ptr(stream))
+    if rc != _native.NXT_PA_OK:
+        raise PagedAttentionError(rc, "nxt_build_block_tables")
+    return BlockTables(buf, list(offsets), B, int(max_blocks), (g[0], g[1], g[2]))

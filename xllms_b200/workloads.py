@@ -44,6 +44,7 @@ class PagedBatch:
     rank: int = 0
     total_heads: int = 0    # query heads across all ranks
     notes: dict = field(default_factory=dict)
+    kv_elem_size: int = 0   # bytes per K/V element when the cache is quantised (0: elem_size)
     # shared radix prefixes: (member sequence ids, shared leading pages) per group
     prefix_groups: list = field(default_factory=list)
 
@@ -74,10 +75,14 @@ class PagedBatch:
     def pages_per_seq(self) -> np.ndarray:
         return (self.seq_lens.astype(np.int64) + self.block_size - 1) // self.block_size
 
+    @property
+    def kv_es(self) -> int:
+        return self.kv_elem_size or self.elem_size
+
     def kv_bytes(self) -> int:
         """K+V bytes the attention reads, counted per sequence (logical)."""
         return int(self.seq_lens.astype(np.int64).sum()) * self.num_kv_heads * \
-            self.head_size * 2 * self.elem_size
+            self.head_size * 2 * self.kv_es
 
     def kv_bytes_unique(self) -> int:
         """K+V bytes of distinct (page, slot) cells read: shared prefix pages count once."""
@@ -90,7 +95,7 @@ class PagedBatch:
                 n = min(self.block_size, L - j * self.block_size)
                 if used.get(phys, 0) < n:
                     used[phys] = n
-        return sum(used.values()) * self.num_kv_heads * self.head_size * 2 * self.elem_size
+        return sum(used.values()) * self.num_kv_heads * self.head_size * 2 * self.kv_es
 
     def algorithmic_bytes(self, unique: bool = False) -> int:
         """KV bytes + Q + out + block-table entries read + seq_lens."""
@@ -141,6 +146,30 @@ class PagedBatch:
                                              dtype=torch.float32) * self.value_std).to(td)
             out.append(x)
         return tuple(out)
+
+    def values_torch_fp8(self, device, fmt: str = "e4m3"):
+        """Q (fp16) and K, V pools quantised to fp8 with one scale per pool
+        (max |x| maps to the format's largest value): (q, k8, v8, k_scale,
+        v_scale), the pools as uint8 tensors holding encode(x / scale)."""
+        import torch
+        q, k, v = self.values_torch(device)
+        tdt, fmax = {"e4m3": (torch.float8_e4m3fn, 448.0), "e5m2": (torch.float8_e5m2, 57344.0)}[fmt]
+        out = [q]
+        scales = []
+        for pool in (k, v):
+            sc = float(pool.abs().max().float()) / fmax
+            flat = pool.view(-1)
+            q8 = torch.empty(pool.shape, dtype=torch.uint8, device=device)
+            q8f = q8.view(-1)
+            step = 1 << 27
+            for i in range(0, flat.numel(), step):  # chunks bound the fp32 temporary
+                q8f[i:i + step] = (flat[i:i + step].float() / sc).to(tdt).view(torch.uint8)
+            out.append(q8)
+            scales.append(sc)
+            del pool
+        self.kv_elem_size = 1
+        self.notes.update(kv_format=fmt, k_scale=scales[0], v_scale=scales[1])
+        return out[0], out[1], out[2], scales[0], scales[1]
 
     def tables_torch(self, device):
         import torch
