@@ -346,26 +346,42 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
       float sc[NT][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      if constexpr (KVF != 0) {
+        // fp8 rows of 128 bytes, 16-byte chunk ks % 8 of box ks / 8 (chunk
+        // index XOR row % 8); lane (g, c) reads 4 bytes of tokens g, g + 8.
+        // All loads first, then two independent accumulation chains.
+        uint32_t kw[C::kKSteps][2];
 #pragma unroll
-      for (int ks = 0; ks < C::kKSteps; ++ks) {
-        uint32_t a0, a1, a2, a3;
-        if constexpr (KVF != 0) {
-          // fp8 rows of 128 bytes, 16-byte chunk ks % 8 of box ks / 8 (chunk
-          // index XOR row % 8); lane (g, c) reads 4 bytes of tokens g, g + 8
+        for (int ks = 0; ks < C::kKSteps; ++ks) {
           const uint32_t off = (uint32_t)((ks >> 3) * 2048 + (((ks & 7) ^ g) << 4) + 4 * c);
-          uint32_t w0, w1;
-          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w0) : "r"(tk + off + g * 128));
-          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w1) : "r"(tk + off + (g + 8) * 128));
-          a0 = fp8x2_to_h2<KVF>(w0);
-          a2 = fp8x2_to_h2<KVF>(w0 >> 16);
-          a1 = fp8x2_to_h2<KVF>(w1);
-          a3 = fp8x2_to_h2<KVF>(w1 >> 16);
-        } else {
-          ldsm_x4(tk + tile_off(r8 + ((mi & 1) << 3), 2 * ks + (mi >> 1)), a0, a1, a2, a3);
+          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(kw[ks][0]) : "r"(tk + off + g * 128));
+          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(kw[ks][1]) : "r"(tk + off + (g + 8) * 128));
+        }
+        float sc2[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) sc2[nt][0] = sc2[nt][1] = sc2[nt][2] = sc2[nt][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < C::kKSteps; ++ks) {
+          const uint32_t a0 = fp8x2_to_h2<KVF>(kw[ks][0]), a2 = fp8x2_to_h2<KVF>(kw[ks][0] >> 16);
+          const uint32_t a1 = fp8x2_to_h2<KVF>(kw[ks][1]), a3 = fp8x2_to_h2<KVF>(kw[ks][1] >> 16);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            mma_f16_16816((ks & 1) ? sc2[nt] : sc[nt], a0, a1, a2, a3, qf[nt][ks][0],
+                          qf[nt][ks][1]);
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
-          mma_f16_16816(sc[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) sc[nt][r] += sc2[nt][r];
+      } else {
+#pragma unroll
+        for (int ks = 0; ks < C::kKSteps; ++ks) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(tk + tile_off(r8 + ((mi & 1) << 3), 2 * ks + (mi >> 1)), a0, a1, a2, a3);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            mma_f16_16816(sc[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
+        }
       }
 
       // fp8 cache: widen the V page into this warp's fp16 tile (rows >=
@@ -376,14 +392,22 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
         vsrc = sbase + C::kRing + warp * (16 * D * 2);
         constexpr int CH8 = D / 16;  // 16-byte fp8 chunks per row
         // lanes of one 8-lane store phase take 8 rows of one chunk column:
-        // distinct swizzled 16-byte slots, no bank conflicts
-        for (int qi = lane; qi < 16 * CH8; qi += 32) {
-          const int row = qi & 15, c8 = qi >> 4;
-          uint4 w = make_uint4(0u, 0u, 0u, 0u);
-          if (row < ntok)
-            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
-                         : "r"(tv + (c8 >> 3) * 2048 + row * 128 + (((c8 & 7) ^ (row & 7)) << 4)));
+        // distinct swizzled 16-byte slots, no bank conflicts. Every load is
+        // issued before the first conversion.
+        constexpr int ITER = 16 * CH8 / 32;
+        uint4 wv[ITER];
+#pragma unroll
+        for (int i = 0; i < ITER; ++i) {
+          const int qi = lane + 32 * i, row = qi & 15, c8 = qi >> 4;
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(wv[i].x), "=r"(wv[i].y), "=r"(wv[i].z), "=r"(wv[i].w)
+                       : "r"(tv + (c8 >> 3) * 2048 + row * 128 + (((c8 & 7) ^ (row & 7)) << 4)));
+          if (row >= ntok) wv[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < ITER; ++i) {
+          const int qi = lane + 32 * i, row = qi & 15, c8 = qi >> 4;
+          const uint4 w = wv[i];
           const uint32_t h0 = fp8x2_to_h2<KVF>(w.x), h1 = fp8x2_to_h2<KVF>(w.x >> 16);
           const uint32_t h2 = fp8x2_to_h2<KVF>(w.y), h3 = fp8x2_to_h2<KVF>(w.y >> 16);
           const uint32_t h4 = fp8x2_to_h2<KVF>(w.z), h5 = fp8x2_to_h2<KVF>(w.z >> 16);
@@ -564,7 +588,7 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
 }
 
 #ifndef XPA_FP8_MIN_CTAS
-#define XPA_FP8_MIN_CTAS 1
+#define XPA_FP8_MIN_CTAS 5
 #endif
 template <int D, int NT, int STAGES, int NWC, int KVF>
 __global__ void __launch_bounds__((NWC + 1) * 32, KVF ? XPA_FP8_MIN_CTAS : 1)
@@ -799,12 +823,22 @@ cudaError_t launch_generic_typed(const Params& p, cudaStream_t st) {
 #define XPA_CONSUMER_WARPS 2
 #endif
 
+// fp8 caches: pages are half the bytes, so a CTA needs twice the page rate.
+#ifndef XPA_FP8_RING_PAGES
+#define XPA_FP8_RING_PAGES 6
+#endif
+#ifndef XPA_FP8_CONSUMER_WARPS
+#define XPA_FP8_CONSUMER_WARPS 2
+#endif
+
 template <int D, int NT, int KVF>
 cudaError_t launch_fast_t(const CUtensorMap& tk, const CUtensorMap& tv, const Params& p,
                           cudaStream_t st) {
-  constexpr int STAGES = (D == 256) ? (XPA_RING_PAGES / 2 > 1 ? XPA_RING_PAGES / 2 : 2)
-                                    : XPA_RING_PAGES;
-  constexpr int NWC = XPA_CONSUMER_WARPS;
+  constexpr int RING = KVF ? XPA_FP8_RING_PAGES : XPA_RING_PAGES;
+  constexpr int NWC = KVF ? XPA_FP8_CONSUMER_WARPS : XPA_CONSUMER_WARPS;
+  // D = 256 pages are twice as large: half the ring, still a multiple of NWC
+  constexpr int HALF = RING / 2 > NWC ? RING / 2 : NWC;
+  constexpr int STAGES = (D == 256) ? (HALF + NWC - 1) / NWC * NWC : RING;
   using C = FastCfg<D, NT, STAGES, NWC, KVF>;
   auto kern = pa_tma_mma_kernel<D, NT, STAGES, NWC, KVF>;
   // The attribute is per function and device; setting it every call costs
