@@ -416,37 +416,6 @@ __device__ __forceinline__ void store_out8(const Params& p, long long row, int d
   }
 }
 
-// Stores elements d0 .. d0+3 of output row `row`: one 8-byte (fp16) or
-// 16-byte (fp32) store per destination. Requires Params::vec8.
-template <typename T>
-__device__ __forceinline__ void store_out4(const Params& p, long long row, int d0, float4 v) {
-  long long off;
-  if (p.npeers == 0) {
-    off = row * p.D + d0;
-  } else {
-    const long long b = row / p.Hq, h = row - b * p.Hq;
-    off = p.peer_off + (b * p.Hq_total + p.head_offset + h) * p.D + d0;
-  }
-  if constexpr (sizeof(T) == 2) {
-    const uint2 u = make_uint2(pack_half2(v.x, v.y), pack_half2(v.z, v.w));
-    if (p.npeers == 0) {
-      *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + off) = u;
-      return;
-    }
-#pragma unroll
-    for (int r = 0; r < kMaxPeers; ++r)
-      if (r < p.npeers) *reinterpret_cast<uint2*>(static_cast<__half*>(p.peers[r]) + off) = u;
-  } else {
-    if (p.npeers == 0) {
-      *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off) = v;
-      return;
-    }
-#pragma unroll
-    for (int r = 0; r < kMaxPeers; ++r)
-      if (r < p.npeers) *reinterpret_cast<float4*>(static_cast<float*>(p.peers[r]) + off) = v;
-  }
-}
-
 // ── split-context merge ─────────────────────────────────────────────────
 // Log-sum-exp merge of the partials (slots) of one (b, q head) row into out,
 // by one warp:
@@ -454,7 +423,8 @@ __device__ __forceinline__ void store_out4(const Params& p, long long row, int d
 // Lane i holds slot i's (m, l) (slots past 32 are re-read from L2); the
 // weights of the first 32 slots go to the warp's 32 floats of shared memory
 // `sw`. Each lane then accumulates 4 consecutive output elements (1 without
-// vec8) over the slots, four slots' loads in flight at a time. Partials were
+// vec8) over the slots, four slots' loads in flight at a time; with vec8 the
+// even lane of each pair stores the pair's 8 elements in one 16-byte store. Partials were
 // written by other CTAs, so they are read through L2 (ld.global.cg).
 template <typename T>
 __device__ __forceinline__ void merge_row_warp(const Params& p, long long row, int nslots,
@@ -477,40 +447,56 @@ __device__ __forceinline__ void merge_row_warp(const Params& p, long long row, i
   auto wt = [&](int i) { return i < 32 ? sw[i] : weight(__ldcg(&ml[i].x)); };
   const float* po = p.part_o + row * p.slots * p.D;
   if (p.vec8) {
-    for (int d0 = lane * 4; d0 < p.D; d0 += 128) {
+    // Every lane runs every 128-element pass (lanes past D load nothing), so
+    // the pair shuffles below have the whole warp.
+    for (int base = 0; base < p.D; base += 128) {
+      const int d0 = base + lane * 4;
+      const bool act = d0 < p.D;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      int i = 0;
-      for (; i + 4 <= nslots; i += 4) {
-        float4 x[4];
+      if (act) {
+        int i = 0;
+        for (; i + 4 <= nslots; i += 4) {
+          float4 x[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          x[u] = __ldcg(reinterpret_cast<const float4*>(po + (long long)(i + u) * p.D + d0));
+          for (int u = 0; u < 4; ++u)
+            x[u] = __ldcg(reinterpret_cast<const float4*>(po + (long long)(i + u) * p.D + d0));
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float w = wt(i + u);
-          acc.x = fmaf(w, x[u].x, acc.x);
-          acc.y = fmaf(w, x[u].y, acc.y);
-          acc.z = fmaf(w, x[u].z, acc.z);
-          acc.w = fmaf(w, x[u].w, acc.w);
+          for (int u = 0; u < 4; ++u) {
+            const float w = wt(i + u);
+            acc.x = fmaf(w, x[u].x, acc.x);
+            acc.y = fmaf(w, x[u].y, acc.y);
+            acc.z = fmaf(w, x[u].z, acc.z);
+            acc.w = fmaf(w, x[u].w, acc.w);
+          }
+        }
+        for (; i < nslots; ++i) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(po + (long long)i * p.D + d0));
+          const float w = wt(i);
+          acc.x = fmaf(w, x.x, acc.x);
+          acc.y = fmaf(w, x.y, acc.y);
+          acc.z = fmaf(w, x.z, acc.z);
+          acc.w = fmaf(w, x.w, acc.w);
+        }
+        if (tot > 0.f) {
+          acc.x /= tot;
+          acc.y /= tot;
+          acc.z /= tot;
+          acc.w /= tot;
+        } else {
+          acc = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
-      for (; i < nslots; ++i) {
-        const float4 x = __ldcg(reinterpret_cast<const float4*>(po + (long long)i * p.D + d0));
-        const float w = wt(i);
-        acc.x = fmaf(w, x.x, acc.x);
-        acc.y = fmaf(w, x.y, acc.y);
-        acc.z = fmaf(w, x.z, acc.z);
-        acc.w = fmaf(w, x.w, acc.w);
+      // even lanes take their odd neighbour's 4 elements and store 8 at once
+      // (16-byte stores: half the transactions, which counts most for the
+      // peer stores of the fused head gather); D % 8 == 0 keeps pairs whole
+      const float4 nb = make_float4(__shfl_down_sync(0xffffffffu, acc.x, 1),
+                                    __shfl_down_sync(0xffffffffu, acc.y, 1),
+                                    __shfl_down_sync(0xffffffffu, acc.z, 1),
+                                    __shfl_down_sync(0xffffffffu, acc.w, 1));
+      if (act && (lane & 1) == 0) {
+        const float v8[8] = {acc.x, acc.y, acc.z, acc.w, nb.x, nb.y, nb.z, nb.w};
+        store_out8<T>(p, row, d0, v8);
       }
-      if (tot > 0.f) {
-        acc.x /= tot;
-        acc.y /= tot;
-        acc.z /= tot;
-        acc.w /= tot;
-      } else {
-        acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      store_out4<T>(p, row, d0, acc);
     }
   } else {
     for (int d = lane; d < p.D; d += 32) {

@@ -587,11 +587,20 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
   }
 }
 
+// Resident CTAs per SM the register allocation must allow, for D <= 128 with
+// one 8-head tile: 6 for fp16 pages (the shared-memory limit of the 4-page
+// ring), 5 for fp8 pages. The wider variants (D = 256, 16 heads per KV head)
+// keep their registers instead: a bound would spill them.
+#ifndef XPA_FP16_MIN_CTAS
+#define XPA_FP16_MIN_CTAS 6
+#endif
 #ifndef XPA_FP8_MIN_CTAS
 #define XPA_FP8_MIN_CTAS 5
 #endif
 template <int D, int NT, int STAGES, int NWC, int KVF>
-__global__ void __launch_bounds__((NWC + 1) * 32, KVF ? XPA_FP8_MIN_CTAS : 1)
+__global__ void __launch_bounds__((NWC + 1) * 32,
+                                  (D <= 128 && NT == 1) ? (KVF ? XPA_FP8_MIN_CTAS : XPA_FP16_MIN_CTAS)
+                                                        : 1)
     pa_tma_mma_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const Params p) {
   tma_mma_body<D, NT, STAGES, NWC, KVF>(tmK, tmV, p);
