@@ -203,7 +203,7 @@ int nxt_paged_attention_noalloc(
  * tiny budget makes the waits run out on purpose without faulting the GPU. */
 uint64_t nxt_paged_attention_set_wait_budget_ns(uint64_t budget_ns);
 
-/* ── extension: KV append (SURVEY row f1; no paged writer exists in the
+/* ── extension: KV append (no paged writer exists in the
  * reference, whose decode loop memcpy's each token into a contiguous cache,
  * examples/text_gen.c:1274-1278) ──────────────────────────────────────
  * Writes token t's key and value rows (key/value[t*token_stride + h*head_size
