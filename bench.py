@@ -48,6 +48,9 @@ def parse_args():
     ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "c5", "act"], default="c2",
                     help="c1..c5: the paged-attention configurations; act: one activation "
                          "operator (--act-op) on a Llama-3-8B MLP-sized input, 1 GPU")
+    ap.add_argument("--graph", action="store_true",
+                    help="1 GPU: capture one step in a CUDA graph and time K replays "
+                         "(device time of launch-bound small configurations such as c1)")
     ap.add_argument("--kv", choices=["fp16", "e4m3", "e5m2"], default="fp16",
                     help="KV cache format (c2/c3/c5, 1 GPU): e4m3 / e5m2 = fp8 pools with one "
                          "scale per pool (nxt_paged_attention_fp8_ex)")
@@ -378,13 +381,35 @@ def run_ours(args, rank, world, local_rank):
         raise SystemExit(f"device status after warm-up: {st:#x}")
 
     K = args.steps
-    # Timed region 1: K plain steps -> value, ms_per_step, clocks.
+    # Timed region 1: K plain steps -> value, ms_per_step, clocks. With
+    # --graph the step is captured once and replayed K times (same kernels,
+    # no host launch work between them).
+    graph = None
+    if args.graph:
+        if world > 1:
+            raise SystemExit("--graph is a 1-GPU option")
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()  # a call on the capture stream before capturing
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        # capture on the stream that already holds the library's workspace
+        # (allocating one would not be allowed while capturing)
+        with torch.cuda.graph(graph, stream=side):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     c0 = ClockSampler.now()
     start.record()
     for _ in range(K):
-        step()
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
     stop.record()
     barrier()
     c1 = ClockSampler.now()
@@ -559,6 +584,7 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
                             f"KV-head sharding x{world} + NCCL all-gather of outputs"),
             "l2": f"no flush: each step reads {tot_kv / world / 1e9:.2f} GB of KV per GPU "
                   f"(> {L2_BYTES >> 20} MB L2)",
+            "timing": "CUDA graph of one step, K replays" if args.graph else "K enqueued steps",
             "path": {1: "tma_mma", 2: "generic"}.get(path, "none") +
                     (" + shared-prefix (cascade) kernel" if cascade else "") +
                     (" (fp8 KV variant)" if batch.kv_elem_size == 1 else ""),

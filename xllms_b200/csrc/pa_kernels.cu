@@ -81,35 +81,63 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
       l[j] = 0.f;
     }
 
-    for (int t = t_begin + w; t < t_end; t += NW) {
-      const int phys = __ldg(bt_row + t / p.block_size);
-      if (phys < 0 || (p.num_blocks > 0 && phys >= p.num_blocks)) {
-        if (lane == 0 && hg0 == 0) raise_status(p, kDevBadPage);
-        continue;
-      }
-      const long long base = (long long)phys * p.kv_block_stride +
-                             (long long)it.kvh * p.kv_head_stride +
-                             (long long)(t % p.block_size) * D;
-      float kf[DPL], vf[DPL];
+    // Tokens w, w + NW, ... of the item, U at a time: the K / V loads of U
+    // tokens are in flight together and their U dot products reduce in
+    // independent butterflies, instead of one HBM round trip per token.
+    constexpr int U = DPL <= 4 ? 4 : 2;
+    for (int t0 = t_begin + w; t0 < t_end; t0 += NW * U) {
+      float kf[U][DPL], vf[U][DPL];
+      bool ok[U];
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) {
-        const int d = lane + 32 * i;
-        kf[i] = d < D ? kv_load<T, KVF>(p.k, base + d) : 0.f;
-        vf[i] = d < D ? kv_load<T, KVF>(p.v, base + d) * vs : 0.f;
+      for (int u = 0; u < U; ++u) {
+        const int t = t0 + u * NW;
+        ok[u] = false;
+        if (t < t_end) {
+          const int phys = __ldg(bt_row + t / p.block_size);
+          if (phys < 0 || (p.num_blocks > 0 && phys >= p.num_blocks)) {
+            if (lane == 0 && hg0 == 0) raise_status(p, kDevBadPage);
+          } else {
+            ok[u] = true;
+          }
+          const long long base = (long long)(ok[u] ? phys : 0) * p.kv_block_stride +
+                                 (long long)it.kvh * p.kv_head_stride +
+                                 (long long)(t % p.block_size) * D;
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) {
+            const int d = lane + 32 * i;
+            kf[u][i] = (ok[u] && d < D) ? kv_load<T, KVF>(p.k, base + d) : 0.f;
+            vf[u][i] = (ok[u] && d < D) ? kv_load<T, KVF>(p.v, base + d) * vs : 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) kf[u][i] = vf[u][i] = 0.f;
+        }
       }
 #pragma unroll
       for (int j = 0; j < HG; ++j) {
-        float dot = 0.f;
+        float dot[U];
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) dot = fmaf(q[j][i], kf[i], dot);
-        const float s = warp_sum(dot) * p.scale_log2;
-        const float mn = fmaxf(m[j], s);
-        const float alpha = ex2(m[j] - mn);
-        const float pj = ex2(s - mn);
-        l[j] = fmaf(l[j], alpha, pj);
+        for (int u = 0; u < U; ++u) {
+          dot[u] = 0.f;
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) o[j][i] = fmaf(o[j][i], alpha, pj * vf[i]);
-        m[j] = mn;
+          for (int i = 0; i < DPL; ++i) dot[u] = fmaf(q[j][i], kf[u][i], dot[u]);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+          for (int u = 0; u < U; ++u) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], off);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (!ok[u]) continue;  // the same for every lane
+          const float sv = dot[u] * p.scale_log2;
+          const float mn = fmaxf(m[j], sv);
+          const float alpha = ex2(m[j] - mn);
+          const float pj = ex2(sv - mn);
+          l[j] = fmaf(l[j], alpha, pj);
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) o[j][i] = fmaf(o[j][i], alpha, pj * vf[u][i]);
+          m[j] = mn;
+        }
       }
     }
 
