@@ -245,7 +245,8 @@ int nxt_paged_attention_append_ex(
  * output are fp16; strides are in elements (= bytes). Head sizes 128 and 256
  * with page size 16 take the TMA + tensor-core path; every other shape the
  * CUDA-core kernel. Results are those of nxt_paged_attention_ex over the
- * dequantised cache. */
+ * dequantised cache. A caller-owned workspace needs
+ * nxt_paged_attention_fp8_workspace_size bytes. */
 #define NXT_KV_FP8_E4M3 1 /* 4 exponent bits, no infinities, max 448   */
 #define NXT_KV_FP8_E5M2 2 /* 5 exponent bits, max 57344                 */
 
@@ -262,6 +263,12 @@ int nxt_paged_attention_fp8_ex(
     void *workspace, size_t workspace_bytes,
     int *device_status,
     nxt_stream_t stream);
+
+/* Workspace bytes a nxt_paged_attention_fp8_ex call with these sizes needs
+ * (fp8 pools may take shorter context partitions than fp16 ones). */
+size_t nxt_paged_attention_fp8_workspace_size(int num_seqs, int num_heads, int head_size,
+                                              int num_kv_heads, int max_num_blocks_per_seq,
+                                              int block_size);
 
 /* KV append into fp8 pools: fp16 key/value rows ([num_tokens][num_kv_heads]
  * [head_size] at token_stride) are stored at slot_mapping[t] as

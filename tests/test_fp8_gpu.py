@@ -104,3 +104,23 @@ def test_fp8_append_bit_exact(cuda, name, fmt, fmax, head_size):
     O.reshape_and_cache(k8, v8, kc, vc, slots, block_size=bs)
     assert np.array_equal(kcd.cpu().numpy(), kc)
     assert np.array_equal(vcd.cpu().numpy(), vc)
+
+
+def test_fp8_caller_workspace(cuda):
+    import torch
+    b = W.make_batch("f8w", [5000, 3000, 40], 8, 2, 128, "f16", 325)
+    q, k8, v8, ks, vs = _quantised(b, O.FP8_E4M3, 448.0)
+    need = _native.xpa().nxt_paged_attention_fp8_workspace_size(
+        b.num_seqs, b.num_heads, b.head_size, b.num_kv_heads, b.max_blocks, b.block_size)
+    assert need > 0
+    bt, sl = b.tables_torch(cuda)
+    args = (torch.from_numpy(q).to(cuda), torch.from_numpy(k8).to(cuda),
+            torch.from_numpy(v8).to(cuda), bt, sl, "e4m3", ks, vs)
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda)
+    out = PA.paged_attention_fp8(*args, scale=b.scale, workspace=ws)
+    ref = O.attention_fp8(q, k8, v8, O.FP8_E4M3, ks, vs, b.block_tables, b.seq_lens,
+                          b.num_kv_heads, b.scale, f64=True)
+    check_close(out, ref, what="fp8 caller workspace")
+    with pytest.raises(PA.PagedAttentionError) as e:
+        PA.paged_attention_fp8(*args, scale=b.scale, workspace=ws[:need - 1])
+    assert e.value.code == _native.NXT_PA_EWORKSPACE

@@ -94,6 +94,7 @@ SIGNATURES = {
         _I,
         [_VP, _CVP, _CVP, _CVP, _IP, _IP, _I, _I, _I, _I, _F, _I, _I, _I, _F, _F, _I64, _I64,
          _I64, _VP, _SZ, _VP, _VP]),
+    "nxt_paged_attention_fp8_workspace_size": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "nxt_reshape_and_cache_fp8": (
         _I, [_CVP, _CVP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _F, _I64, _I64, _I64, _VP]),
     "nxt_reshape_and_cache": (

@@ -111,11 +111,19 @@ int sm_count_of(int dev) {
 #define XPA_PART_PAGES 128
 #endif
 
-Plan make_plan(int B, int Hq, int D, int Hkv, int max_blocks, int nsm) {
+// fp8 pages stream in half the time, so the grid needs more CTAs per SM
+// before partitions stop shrinking (measured at config 2: 128-page
+// partitions 0.1675 ms, 64-page 0.1591 ms; at configs 3 and 5, which already
+// have > 24 CTAs per SM, shorter partitions only add merge work).
+#ifndef XPA_FP8_MIN_ITEMS_PER_SM
+#define XPA_FP8_MIN_ITEMS_PER_SM 24
+#endif
+Plan make_plan(int B, int Hq, int D, int Hkv, int max_blocks, int nsm, int kv_es) {
   Plan pl;
   const long long mb = max_blocks > 0 ? max_blocks : 1;
   int pp = XPA_PART_PAGES;
-  while (pp > 4 && (long long)B * Hkv * ceil_div(mb, pp) < 12LL * nsm) pp >>= 1;
+  const long long min_items = (long long)(kv_es == 1 ? XPA_FP8_MIN_ITEMS_PER_SM : 12) * nsm;
+  while (pp > 4 && (long long)B * Hkv * ceil_div(mb, pp) < min_items) pp >>= 1;
   while (ceil_div(mb, pp) > 8192) pp <<= 1;
   pl.part_pages = pp;
   pl.max_parts = ceil_div(mb, pp);
@@ -265,7 +273,7 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NXT_PA_ECUDA;
-  Plan pl = make_plan(B, Hq, D, Hkv, max_blocks, sm_count_of(dev));
+  Plan pl = make_plan(B, Hq, D, Hkv, max_blocks, sm_count_of(dev), kv_es);
   // A cascade call needs the TMA path's shapes; others run without the prefix
   // information, which gives the same result.
   CUtensorMap tk, tv;
@@ -493,6 +501,18 @@ size_t nxt_paged_attention_workspace_size(int num_seqs, int num_heads, int head_
   if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
   return make_plan(num_seqs, num_heads, head_size, num_kv_heads, max_num_blocks_per_seq,
                    sm_count_of(dev))
+      .ws_bytes;
+}
+
+size_t nxt_paged_attention_fp8_workspace_size(int num_seqs, int num_heads, int head_size,
+                                              int num_kv_heads, int max_num_blocks_per_seq,
+                                              int block_size) {
+  (void)block_size;
+  if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0 || head_size <= 0) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  return make_plan(num_seqs, num_heads, head_size, num_kv_heads, max_num_blocks_per_seq,
+                   sm_count_of(dev), 1)
       .ws_bytes;
 }
 

@@ -19,7 +19,9 @@ struct Plan {
   int max_parts = 1;
   size_t ws_bytes = 0;
 };
-Plan make_plan(int B, int Hq, int D, int Hkv, int max_blocks, int nsm);
+// kv_es: bytes per K / V element (1 for fp8 pools, whose partitions keep
+// shrinking until the grid holds 24 CTAs per SM instead of 12).
+Plan make_plan(int B, int Hq, int D, int Hkv, int max_blocks, int nsm, int kv_es = 2);
 
 // Tensor map of one pool for the TMA path; false when it cannot be encoded.
 // es: bytes per K / V element (2 = fp16, 1 = fp8).

@@ -199,6 +199,12 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
 // Bound on the producer's wait for its own in-flight copies after a timeout.
 constexpr uint64_t kDrainBudgetNs = 1000000000ull;
 
+// fp8 pages: the producer also prefetches, into L2, the page this many
+// positions ahead of the one it loads (0: off).
+#ifndef XPA_FP8_L2_AHEAD
+#define XPA_FP8_L2_AHEAD 0
+#endif
+
 template <int D, int NT, int STAGES, int NWC, int KVF>
 struct FastCfg {
   static constexpr int kElem = KVF ? 1 : 2;      // bytes per K / V element
@@ -269,12 +275,34 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
     int ent = -1;
     int ok = 1, issued = 0;
     const int last_page = (it.L + 15) / 16 - 1;  // holds an appended token
+    // fp8 pages: L2 prefetch of the page kAhead positions further on, so
+    // more bytes are on their way from HBM than the ring can hold
+    constexpr int kAhead = KVF ? XPA_FP8_L2_AHEAD : 0;
+    int entp = -1, pbase = -1 - 32;
     for (int j = 0; j < np; ++j) {
       if ((j & 31) == 0) {
         const int idx = it.page_begin + j + lane;
         ent = idx < it.page_end ? __ldg(bt_row + idx) : -1;
       }
       const int phys = __shfl_sync(0xffffffffu, ent, j & 31);
+      if constexpr (kAhead > 0) {
+        const int jp = j + kAhead;
+        if (jp >= STAGES && jp < np) {  // pages below STAGES load at once anyway
+          if (jp >= pbase + 32) {
+            pbase = jp;
+            const int idx = it.page_begin + jp + lane;
+            entp = idx < it.page_end ? __ldg(bt_row + idx) : -1;
+          }
+          const int pp = __shfl_sync(0xffffffffu, entp, jp - pbase);
+          if (lane == 0 && pp >= 0 && (p.num_blocks <= 0 || pp < p.num_blocks)) {
+#pragma unroll
+            for (int x = 0; x < C::kBoxes; ++x) {
+              tma_prefetch_l2_4d(&tmK, x * C::kBoxElems, 0, it.kvh, pp);
+              tma_prefetch_l2_4d(&tmV, x * C::kBoxElems, 0, it.kvh, pp);
+            }
+          }
+        }
+      }
       if (lane == 0) {
         const int s = j % STAGES;
         // Only the page an append kernel wrote into must wait for that kernel.
