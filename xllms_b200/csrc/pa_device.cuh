@@ -258,16 +258,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* tm,
       : "memory");
 }
 
-// Brings one tensor box into L2 ahead of its load (no shared memory, no
-// completion to wait for).
-__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* tm, int c0, int c1, int c2,
-                                                   int c3) {
-  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
-                   reinterpret_cast<uint64_t>(tm)),
-               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-               : "memory");
-}
-
 // Shared-memory byte offset of the 16-byte chunk `chunk` (along d) of token
 // row `tok` in a page tile written by TMA with 128-byte swizzle: the tile is
 // D/64 boxes of 16 rows x 128 bytes, and within each 1024-byte group the

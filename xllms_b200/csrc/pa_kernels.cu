@@ -199,12 +199,6 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
 // Bound on the producer's wait for its own in-flight copies after a timeout.
 constexpr uint64_t kDrainBudgetNs = 1000000000ull;
 
-// fp8 pages: the producer also prefetches, into L2, the page this many
-// positions ahead of the one it loads (0: off).
-#ifndef XPA_FP8_L2_AHEAD
-#define XPA_FP8_L2_AHEAD 0
-#endif
-
 template <int D, int NT, int STAGES, int NWC, int KVF>
 struct FastCfg {
   static constexpr int kElem = KVF ? 1 : 2;      // bytes per K / V element
@@ -266,51 +260,39 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
   const uint64_t budget = p.timeout_ns;
 
   if (warp == NWC) {
-    // ── producer ──────────────────────────────────────────────────────
+    // ── producers: lane k < NWC feeds consumer warp k, i.e. the pages
+    // j = k, k + NWC, ... and their ring stages (STAGES % NWC == 0 gives each
+    // stage one owner), so a consumer that frees its stages late holds up
+    // only its own next page.
     if (lane == 0) {
       tmap_prefetch(&tmK);
       tmap_prefetch(&tmV);
     }
-    const int* bt_row = p.block_tables + (long long)it.b * p.max_blocks;
-    int ent = -1;
-    int ok = 1, issued = 0;
-    const int last_page = (it.L + 15) / 16 - 1;  // holds an appended token
-    // fp8 pages: L2 prefetch of the page kAhead positions further on, so
-    // more bytes are on their way from HBM than the ring can hold
-    constexpr int kAhead = KVF ? XPA_FP8_L2_AHEAD : 0;
-    int entp = -1, pbase = -1 - 32;
-    for (int j = 0; j < np; ++j) {
-      if ((j & 31) == 0) {
-        const int idx = it.page_begin + j + lane;
-        ent = idx < it.page_end ? __ldg(bt_row + idx) : -1;
-      }
-      const int phys = __shfl_sync(0xffffffffu, ent, j & 31);
-      if constexpr (kAhead > 0) {
-        const int jp = j + kAhead;
-        if (jp >= STAGES && jp < np) {  // pages below STAGES load at once anyway
-          if (jp >= pbase + 32) {
-            pbase = jp;
-            const int idx = it.page_begin + jp + lane;
-            entp = idx < it.page_end ? __ldg(bt_row + idx) : -1;
-          }
-          const int pp = __shfl_sync(0xffffffffu, entp, jp - pbase);
-          if (lane == 0 && pp >= 0 && (p.num_blocks <= 0 || pp < p.num_blocks)) {
+    if (lane < NWC) {
+      const int* bt_row = p.block_tables + (long long)it.b * p.max_blocks;
+      bool ok = true;
+      int last = -1;  // this lane's last issued page
+      const int last_page = (it.L + 15) / 16 - 1;  // holds an appended token
+      for (int j0 = lane; ok && j0 < np; j0 += 8 * NWC) {
+        int ent[8];
 #pragma unroll
-            for (int x = 0; x < C::kBoxes; ++x) {
-              tma_prefetch_l2_4d(&tmK, x * C::kBoxElems, 0, it.kvh, pp);
-              tma_prefetch_l2_4d(&tmV, x * C::kBoxElems, 0, it.kvh, pp);
-            }
-          }
+        for (int u = 0; u < 8; ++u) {
+          const int jj = j0 + u * NWC;
+          ent[u] = jj < np ? __ldg(bt_row + it.page_begin + jj) : -1;
         }
-      }
-      if (lane == 0) {
-        const int s = j % STAGES;
-        // Only the page an append kernel wrote into must wait for that kernel.
-        if (p.after_append && it.page_begin + j == last_page) pdl_wait_primary();
-        if (j >= STAGES && !mbar_wait(bar_empty + 8 * s, ((j / STAGES) + 1) & 1, budget)) {
-          raise_status(p, kDevTimeout);
-          ok = 0;
-        } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int jj = j0 + u * NWC;
+          if (jj >= np) break;
+          const int s = jj % STAGES;
+          const int phys = ent[u];
+          // Only the page an append kernel wrote into must wait for that kernel.
+          if (p.after_append && it.page_begin + jj == last_page) pdl_wait_primary();
+          if (jj >= STAGES && !mbar_wait(bar_empty + 8 * s, ((jj / STAGES) + 1) & 1, budget)) {
+            raise_status(p, kDevTimeout);
+            ok = false;
+            break;
+          }
           const bool valid = phys >= 0 && (p.num_blocks <= 0 || phys < p.num_blocks);
           meta[s] = valid ? 1 : 0;
           if (valid) {
@@ -326,17 +308,15 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
             raise_status(p, kDevBadPage);
             mbar_arrive(bar_full + 8 * s);
           }
-          issued = j + 1;
+          last = jj;
         }
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-    }
-    if (!ok && lane == 0) {
-      // Let copies already in flight land before the CTA can retire. The
-      // drain has its own bound, independent of the pipeline-wait budget.
-      for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
-        (void)mbar_wait(bar_full + 8 * (j % STAGES), (j / STAGES) & 1, kDrainBudgetNs);
+      if (!ok) {
+        // Let this lane's copies in flight land before the CTA can retire.
+        // The drain has its own bound, independent of the pipeline budget.
+        for (int jj = last; jj >= 0 && jj > last - STAGES; jj -= NWC)
+          (void)mbar_wait(bar_full + 8 * (jj % STAGES), (jj / STAGES) & 1, kDrainBudgetNs);
+      }
     }
     return;
   }
