@@ -870,7 +870,7 @@ cudaError_t launch_generic_typed(const Params& p, cudaStream_t st) {
 
 // fp8 caches: pages are half the bytes, so a CTA needs twice the page rate.
 #ifndef XPA_FP8_RING_PAGES
-#define XPA_FP8_RING_PAGES 6
+#define XPA_FP8_RING_PAGES 8
 #endif
 #ifndef XPA_FP8_CONSUMER_WARPS
 #define XPA_FP8_CONSUMER_WARPS 2
