@@ -51,9 +51,9 @@ def parse_args():
     ap.add_argument("--graph", action="store_true",
                     help="1 GPU: capture one step in a CUDA graph and time K replays "
                          "(device time of launch-bound small configurations such as c1)")
-    ap.add_argument("--kv", choices=["fp16", "e4m3", "e5m2"], default="fp16",
-                    help="KV cache format (c2/c3/c5, 1 GPU): e4m3 / e5m2 = fp8 pools with one "
-                         "scale per pool (nxt_paged_attention_fp8_ex)")
+    ap.add_argument("--kv", choices=["fp16", "e4m3", "e5m2", "int8"], default="fp16",
+                    help="KV cache format (c2/c3/c5, 1 GPU): e4m3 / e5m2 = fp8 pools, int8 = "
+                         "int8 pools, one scale per pool (nxt_paged_attention_fp8_ex)")
     ap.add_argument("--act-op", default="silu_and_mul",
                     choices=["silu_and_mul", "mul_and_silu", "gelu_and_mul",
                              "gelu_tanh_and_mul", "gelu", "silu"])
@@ -235,22 +235,59 @@ def host_cores() -> int:
         return os.cpu_count() or 1
 
 
+# The reference CPU attention (examples/run_gpt2.c:63) forms a page's offset
+# as the int product page_idx * (page_size * num_heads * head_dim), so its
+# pool must stay below 2^31 elements; the sample also bounds the fp32 copy
+# of each pool it is given (num_heads wide) to REF_SAMPLE_ELEMS elements.
+REF_SAMPLE_ELEMS = 1 << 28
+
+
+def sample_plan(batch, nseq):
+    """(sequences, context lengths) of the CPU sample: the first sequences, up
+    to `nseq`, whose pages fit the reference's pool limit; when the first
+    sequence alone does not fit, its first tokens that do."""
+    bs = batch.block_size
+    cap = max(1, min(2**31 - 1, REF_SAMPLE_ELEMS) // (bs * batch.num_heads * batch.head_size))
+    seqs, lens, pages = [], [], 0
+    for b in range(min(nseq, batch.num_seqs)):
+        L = int(batch.seq_lens[b])
+        npg = -(-L // bs)
+        if pages + npg > cap:
+            if not seqs:
+                seqs.append(b)
+                lens.append(cap * bs)
+            break
+        seqs.append(b)
+        lens.append(L)
+        pages += npg
+    return seqs, lens
+
+
 def sample_arrays(batch, nseq, q_t=None, k_t=None, v_t=None):
-    """Host arrays (q, k, v, block_tables, seq_lens) of the first `nseq`
+    """Host arrays (q, k, v, block_tables, seq_lens) of the sample_plan
     sequences with their pages renumbered compactly: copied from the device
     pools when given, else drawn on the host (numpy PCG64, the batch's seed)."""
     import numpy as np
-    seqs = list(range(min(nseq, batch.num_seqs)))
+    seqs, lens = sample_plan(batch, nseq)
     if q_t is not None:
         sys.path.insert(0, os.path.join(ROOT, "tests"))
         from _helpers import gather_subset
-        return gather_subset(batch, seqs, q_t, k_t, v_t)
+        q, k, v, bt, sl = gather_subset(batch, seqs, q_t, k_t, v_t)
+        if int(sl[0]) > lens[0]:  # one truncated sequence: keep its first pages
+            npg = -(-lens[0] // batch.block_size)
+            k, v, bt = k[:npg], v[:npg], np.ascontiguousarray(bt[:, :npg])
+            sl = np.array(lens, dtype=np.int32)
+        return q, k, v, bt, sl
     from xllms_b200 import workloads as W
-    sub = W.make_batch(batch.name + "_sample", batch.seq_lens[seqs], batch.num_heads,
+    sub = W.make_batch(batch.name + "_sample", np.array(lens), batch.num_heads,
                        batch.num_kv_heads, batch.head_size, batch.dtype, batch.seed,
                        block_size=batch.block_size, slack=0.0, value_std=batch.value_std)
     q, k, v = sub.values_numpy()
     return q, k, v, sub.block_tables, sub.seq_lens
+
+
+def _kv_label(fmt: str) -> str:
+    return "int8" if fmt == "int8" else f"fp8 {fmt}"
 
 
 def cpu_leg(batch, arrays, seconds: float = 0.0, passes: int = 0, warmup: int = 1):
@@ -259,8 +296,8 @@ def cpu_leg(batch, arrays, seconds: float = 0.0, passes: int = 0, warmup: int = 
     import numpy as np
     from oracle import oracle as O
     q, k, v, bt, sl = arrays
-    if batch.kv_elem_size == 1:  # fp8 pools: the CPU path reads the dequantised values
-        fmt = O.FP8_E4M3 if batch.notes["kv_format"] == "e4m3" else O.FP8_E5M2
+    if batch.kv_elem_size == 1:  # one-byte pools: the CPU path reads the dequantised values
+        fmt = {"e4m3": O.FP8_E4M3, "e5m2": O.FP8_E5M2, "int8": O.KV_INT8}[batch.notes["kv_format"]]
         k = O.fp8_decode(k, fmt) * np.float32(batch.notes["k_scale"])
         v = O.fp8_decode(v, fmt) * np.float32(batch.notes["v_scale"])
     nseq = len(sl)
@@ -296,9 +333,12 @@ def cpu_leg(batch, arrays, seconds: float = 0.0, passes: int = 0, warmup: int = 
         one()
         times.append(time.perf_counter() - t0)
     per = statistics.mean(times)
+    cut = int(sl[0]) < int(batch.seq_lens[0])
     info = {"kind": kind, "cores": cores,
             "sample": f"first {nseq} of {batch.num_seqs} sequences "
-                      f"({int(sl.sum())} context tokens, {sub_bytes / 1e6:.1f} MB algorithmic); "
+                      + (f"(sequence 0 cut to its first {int(sl[0])} tokens: the reference "
+                         "forms page offsets in 32-bit int) " if cut else "")
+                      + f"({int(sl.sum())} context tokens, {sub_bytes / 1e6:.1f} MB algorithmic); "
                       f"{what}; {len(times)} timed passes"}
     return sub_bytes / per / 1e9, per, info
 
@@ -316,7 +356,7 @@ def run_ours(args, rank, world, local_rank):
     batch = make_batch(args.workload, world, rank, args.seqs)
     fp8 = args.kv != "fp16"
     if fp8 and (world > 1 or args.workload in ("c1", "c4")):
-        raise SystemExit("--kv fp8 runs configs 2, 3 and 5 on one GPU")
+        raise SystemExit("--kv e4m3 / e5m2 / int8 runs configs 2, 3 and 5 on one GPU")
     if fp8:
         q, k, v, k_scale, v_scale = batch.values_torch_fp8(dev, args.kv)
     else:
@@ -562,10 +602,11 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f16" if batch.kv_elem_size != 1 else
-                 f"f16 (Q, out), fp8 {batch.notes['kv_format']} KV",
+                 f"f16 (Q, out), {_kv_label(batch.notes['kv_format'])} KV",
         "data": "synthetic: seeded block tables/lengths (numpy PCG64); Q/K/V N(0,1)*std "
                 "drawn on the device (torch CUDA generator)" +
-                ("; K/V quantised to fp8 with one scale per pool" if batch.kv_elem_size == 1
+                (f"; K/V quantised to {_kv_label(batch.notes['kv_format'])} with one scale "
+                 "per pool" if batch.kv_elem_size == 1
                  else ""),
         "config": {
             "workload": batch.name,
@@ -587,7 +628,8 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
             "timing": "CUDA graph of one step, K replays" if args.graph else "K enqueued steps",
             "path": {1: "tma_mma", 2: "generic"}.get(path, "none") +
                     (" + shared-prefix (cascade) kernel" if cascade else "") +
-                    (" (fp8 KV variant)" if batch.kv_elem_size == 1 else ""),
+                    (f" ({_kv_label(batch.notes['kv_format'])} KV variant)"
+                     if batch.kv_elem_size == 1 else ""),
             "kv_cache": batch.notes.get("kv_format", "fp16"),
         },
         "pct_hbm_peak": round(100.0 * (tot_ub / world) / (t_step * 1e-3) / 1e9 / peak, 2),
@@ -638,12 +680,13 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
 
 def run_reference(args, rank, world):
     """The reference's own CPU attention on the host cores, on a sample of this
-    arm's workload (the first 8 sequences); rank 0 only, one sample pass per step."""
+    arm's workload (sample_plan: up to the first 8 sequences); rank 0 only, one
+    sample pass per step."""
     if rank != 0:
         return None
     batch = make_batch(args.workload, world, 0, args.seqs)
-    seqs = min(8, batch.num_seqs)
-    arrays = sample_arrays(batch, seqs)
+    arrays = sample_arrays(batch, 8)
+    seqs = len(arrays[4])
     gbs, per, info = cpu_leg(batch, arrays, passes=max(1, args.steps), warmup=args.warmup)
     return {
         "impl": "reference",
@@ -658,7 +701,8 @@ def run_reference(args, rank, world):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic, the ours arm's seeded workload (first 8 sequences, host-drawn values)",
+        "data": "synthetic, the ours arm's seeded workload (the sample's sequences, host-drawn "
+                "values)",
         "config": {"workload": batch.name, "sample_seqs": seqs, "num_heads": batch.total_heads,
                    "num_kv_heads": batch.num_kv_heads * world, "head_size": batch.head_size,
                    "block_size": batch.block_size},

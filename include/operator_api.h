@@ -238,8 +238,9 @@ int nxt_paged_attention_append_ex(
     int *device_status,
     nxt_stream_t stream);
 
-/* ── extension: fp8 KV cache (reference operators/cache.py:16-24 lists
- * "fp8", "fp8_e4m3", "fp8_e5m2" cache dtypes; no kernel there reads them) ──
+/* ── extension: one-byte KV cache (reference operators/cache.py:16-24 lists
+ * "fp8", "fp8_e4m3", "fp8_e5m2" and "int8" cache dtypes; no kernel there
+ * reads them) ──
  * The pools hold one byte per element, encode(x / k_scale) for K and
  * encode(x / v_scale) for V; attention reads decode(byte) * scale. Query and
  * output are fp16; strides are in elements (= bytes). Head sizes 128 and 256
@@ -249,6 +250,7 @@ int nxt_paged_attention_append_ex(
  * nxt_paged_attention_fp8_workspace_size bytes. */
 #define NXT_KV_FP8_E4M3 1 /* 4 exponent bits, no infinities, max 448   */
 #define NXT_KV_FP8_E5M2 2 /* 5 exponent bits, max 57344                 */
+#define NXT_KV_INT8     3 /* two's-complement int8, -128 .. 127          */
 
 int nxt_paged_attention_fp8_ex(
     void *out, const void *query,
@@ -270,10 +272,10 @@ size_t nxt_paged_attention_fp8_workspace_size(int num_seqs, int num_heads, int h
                                               int num_kv_heads, int max_num_blocks_per_seq,
                                               int block_size);
 
-/* KV append into fp8 pools: fp16 key/value rows ([num_tokens][num_kv_heads]
- * [head_size] at token_stride) are stored at slot_mapping[t] as
- * encode(x / scale), rounded to nearest even and saturated at the format's
- * largest finite value (NaN stays NaN). */
+/* KV append into one-byte pools: fp16 key/value rows ([num_tokens]
+ * [num_kv_heads][head_size] at token_stride) are stored at slot_mapping[t]
+ * as encode(x / scale), rounded to nearest even and saturated at the
+ * format's largest finite value (fp8: NaN stays NaN; int8: NaN gives 0). */
 int nxt_reshape_and_cache_fp8(
     const void *key, const void *value,
     void *key_cache, void *value_cache,

@@ -199,11 +199,11 @@ def build_block_tables(page_offsets, page_ids, seq_lens, max_blocks, block_size=
     return tables, slots, pp, go, mem, G, max_size, max_pages
 
 
-FP8_E4M3, FP8_E5M2 = 1, 2
+FP8_E4M3, FP8_E5M2, KV_INT8 = 1, 2, 3  # one-byte KV formats
 
 
 def fp8_decode(codes, fmt) -> np.ndarray:
-    """uint8 codes -> float32 values (exact)."""
+    """uint8 codes -> float32 values (exact); fmt FP8_E4M3, FP8_E5M2 or KV_INT8."""
     c = _as(codes, np.uint8)
     out = np.zeros(c.shape, dtype=np.float32)
     oracle_lib().pa_fp8_decode(_c(out), _c(c), c.size, int(fmt))
@@ -211,7 +211,8 @@ def fp8_decode(codes, fmt) -> np.ndarray:
 
 
 def fp8_encode(x, fmt) -> np.ndarray:
-    """float32 -> uint8 codes (round to nearest even, saturating)."""
+    """float32 -> uint8 codes (round to nearest even, saturating; KV_INT8
+    codes are two's complement and NaN encodes as 0)."""
     x = _as(x, np.float32)
     out = np.zeros(x.shape, dtype=np.uint8)
     oracle_lib().pa_fp8_encode(_c(out), _c(x), x.size, int(fmt))
@@ -220,7 +221,7 @@ def fp8_encode(x, fmt) -> np.ndarray:
 
 def attention_fp8(q, k_codes, v_codes, fmt, k_scale, v_scale, block_tables, seq_lens,
                   num_kv_heads, scale, block_size=16, num_blocks=-1, f64=False) -> np.ndarray:
-    """Attention over an fp8 KV cache: K = decode(k_codes) * k_scale (V alike),
+    """Attention over a one-byte KV cache: K = decode(k_codes) * k_scale (V alike),
     Q widened to fp32; then the same oracle as the fp16 / fp32 paths."""
     k = fp8_decode(k_codes, fmt) * np.float32(k_scale)
     v = fp8_decode(v_codes, fmt) * np.float32(v_scale)

@@ -61,9 +61,11 @@ uint16_t pa_float_to_half(float x) {
     return sign | (uint16_t)h;
 }
 
-/* ── fp8 codecs (OCP 8-bit floating point: E4M3 without infinities, bias 7,
- * max 448, 0x7F / 0xFF NaN; E5M2, bias 15, max 57344, IEEE-style inf/NaN) ── */
+/* ── one-byte codecs (OCP 8-bit floating point: E4M3 without infinities,
+ * bias 7, max 448, 0x7F / 0xFF NaN; E5M2, bias 15, max 57344, IEEE-style
+ * inf/NaN; two's-complement int8) ── */
 static float fp8_decode_one(uint8_t c, int fmt) {
+    if (fmt == PA_KV_INT8) return (float)(int8_t)c;
     const int sign = c >> 7;
     const int M = fmt == PA_FP8_E4M3 ? 3 : 2, bias = fmt == PA_FP8_E4M3 ? 7 : 15;
     const int e = (c & 0x7f) >> M, m = c & ((1 << M) - 1);
@@ -83,6 +85,13 @@ static float fp8_decode_one(uint8_t c, int fmt) {
 /* Round to nearest even, saturating finite values (and infinities) at the
  * largest finite magnitude; NaN stays NaN. */
 static uint8_t fp8_encode_one(float x, int fmt) {
+    if (fmt == PA_KV_INT8) {
+        /* nearbyintf rounds half to even in the default rounding mode */
+        if (isnan(x)) return 0;
+        const float r = nearbyintf(x);
+        const int i = r > 127.0f ? 127 : (r < -128.0f ? -128 : (int)r);
+        return (uint8_t)(int8_t)i;
+    }
     const int M = fmt == PA_FP8_E4M3 ? 3 : 2, bias = fmt == PA_FP8_E4M3 ? 7 : 15;
     const uint8_t max_code = fmt == PA_FP8_E4M3 ? 0x7e : 0x7b;
     const uint8_t nan_code = 0x7f;

@@ -100,13 +100,16 @@ void pa_oracle_reshape_and_cache(const void *key, const void *value, void *key_c
                                  int elem_size, int64_t kv_block_stride,
                                  int64_t kv_head_stride, int64_t token_stride);
 
-/* fp8 formats of a quantised KV cache (fmt): 1 = E4M3 (no infinities, max
- * 448, 0x7F NaN), 2 = E5M2 (max 57344). decode is exact; encode rounds to
- * nearest even and saturates at the largest finite value (as the PTX
- * cvt.rn.satfinite conversions do), NaN stays NaN. A quantised cache holds
+/* One-byte formats of a quantised KV cache (fmt): 1 = fp8 E4M3 (no
+ * infinities, max 448, 0x7F NaN), 2 = fp8 E5M2 (max 57344), 3 = int8
+ * (two's complement). decode is exact; encode rounds to nearest even and
+ * saturates at the largest finite value (as the PTX cvt.rn.satfinite
+ * conversions do); NaN stays NaN in fp8 and encodes as 0 in int8 (as a
+ * float-to-integer conversion does). A quantised cache holds
  * encode(x / scale) and reads back as decode(c) * scale. */
 #define PA_FP8_E4M3 1
 #define PA_FP8_E5M2 2
+#define PA_KV_INT8 3
 void pa_fp8_decode(float *out, const uint8_t *in, int64_t n, int fmt);
 void pa_fp8_encode(uint8_t *out, const float *in, int64_t n, int fmt);
 

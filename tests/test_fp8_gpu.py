@@ -1,4 +1,4 @@
-"""fp8 KV cache on the GPU: attention over E4M3 / E5M2 pools equals the
+"""One-byte KV cache on the GPU: attention over fp8 E4M3 / E5M2 and int8 pools equals the
 oracle over the dequantised pools (fp64 oracle), and
 the quantising append is bit-exact against the oracle's encoder."""
 import numpy as np
@@ -12,7 +12,7 @@ from xllms_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
 
-FMTS = [("e4m3", O.FP8_E4M3, 448.0), ("e5m2", O.FP8_E5M2, 57344.0)]
+FMTS = [("e4m3", O.FP8_E4M3, 448.0), ("e5m2", O.FP8_E5M2, 57344.0), ("int8", O.KV_INT8, 127.0)]
 EDGE_LENS = [0, 1, 15, 16, 17, 511, 512, 513, 1000]
 
 
@@ -58,25 +58,28 @@ def test_fp8_split_context_and_long(cuda, name, fmt, fmax):
     check_close(out, ref, what=f"{name} split")
 
 
-def test_fp8_d256_group16_generic(cuda):
+@pytest.mark.parametrize("name,fmt,fmax", [FMTS[0], FMTS[2]])
+def test_fp8_d256_group16_generic(cuda, name, fmt, fmax):
     b = W.make_batch("f8g", [300, 17], 32, 2, 256, "f16", 322)
-    out, ref = _run(cuda, b, "e4m3", O.FP8_E4M3, 448.0)
-    check_close(out, ref, what="D=256 GS=16")
+    out, ref = _run(cuda, b, name, fmt, fmax)
+    check_close(out, ref, what=f"{name} D=256 GS=16")
 
 
-def test_fp8_other_page_size(cuda):
+@pytest.mark.parametrize("name,fmt,fmax", [FMTS[1], FMTS[2]])
+def test_fp8_other_page_size(cuda, name, fmt, fmax):
     b = W.make_batch("f8p", [1, 31, 32, 33, 700], 8, 2, 128, "f16", 323, block_size=32)
-    out, ref = _run(cuda, b, "e5m2", O.FP8_E5M2, 57344.0)
-    check_close(out, ref, what="block_size 32")
+    out, ref = _run(cuda, b, name, fmt, fmax)
+    check_close(out, ref, what=f"{name} block_size 32")
 
 
-def test_fp8_bad_pages_masked(cuda):
+@pytest.mark.parametrize("name,fmt,fmax", [FMTS[0], FMTS[2]])
+def test_fp8_bad_pages_masked(cuda, name, fmt, fmax):
     b = W.make_batch("f8b", [200, 64, 90], 8, 2, 128, "f16", 324)
     b.block_tables = b.block_tables.copy()
     b.block_tables[0, 3] = -1
     b.block_tables[2, 1] = b.num_blocks + 5
     PA.device_status(clear=True)
-    out, ref = _run(cuda, b, "e4m3", O.FP8_E4M3, 448.0, num_blocks=b.num_blocks)
+    out, ref = _run(cuda, b, name, fmt, fmax, num_blocks=b.num_blocks)
     check_close(out, ref, what="bad pages")
     assert PA.device_status(clear=True) & _native.NXT_PA_DEV_BAD_PAGE
 

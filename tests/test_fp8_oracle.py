@@ -1,5 +1,6 @@
-"""fp8 KV codec of the oracle, pinned against torch's float8 types, and the
-fp8 C-ABI argument checks (no GPU work)."""
+"""One-byte KV codecs of the oracle (fp8 pinned against torch's float8
+types, int8 against torch's round-half-even and clamp), and the one-byte
+C-ABI argument checks (no GPU work)."""
 import numpy as np
 import pytest
 
@@ -58,7 +59,8 @@ def test_fp8_abi_argument_checks_without_gpu():
     sl = np.ones(1, dtype=np.int32)
     args = lambda fmt, ks, vs: (p, p, p, p, bt.ctypes.data, sl.ctypes.data, 1, 1, 16, 1, 1.0,
                                 1, 16, fmt, ks, vs, 256, 256, 1, None, 0, None, None)
-    assert lib.nxt_paged_attention_fp8_ex(*args(3, 1.0, 1.0)) == einval   # format
+    assert lib.nxt_paged_attention_fp8_ex(*args(4, 1.0, 1.0)) == einval   # format
+    assert lib.nxt_paged_attention_fp8_ex(*args(0, 1.0, 1.0)) == einval
     assert lib.nxt_paged_attention_fp8_ex(*args(1, 0.0, 1.0)) == einval   # scale
     assert lib.nxt_paged_attention_fp8_ex(*args(1, 1.0, float("nan"))) == einval
     sm = np.zeros(1, dtype=np.int64)
@@ -68,3 +70,19 @@ def test_fp8_abi_argument_checks_without_gpu():
                                          256, 256, 16, None) == einval
     assert lib.nxt_reshape_and_cache_fp8(None, None, None, None, None, 0, 1, 16, 16, 1, 1.0, 1.0,
                                          256, 256, 16, None) == _native.NXT_PA_OK
+
+
+def test_int8_codec():
+    codes = np.arange(256, dtype=np.uint8)
+    assert np.array_equal(O.fp8_decode(codes, O.KV_INT8), codes.view(np.int8).astype(np.float32))
+    assert np.array_equal(O.fp8_encode(O.fp8_decode(codes, O.KV_INT8), O.KV_INT8), codes)
+    rng = np.random.default_rng(8)
+    x = (rng.standard_normal(200000) * 60).astype(np.float32)
+    ref = torch.from_numpy(x).round().clamp(-128, 127).to(torch.int8).view(torch.uint8).numpy()
+    assert np.array_equal(O.fp8_encode(x, O.KV_INT8), ref)
+    ties = np.array([0.5, 1.5, 2.5, -0.5, -1.5, 126.5, -127.5, 127.5, -128.5], np.float32)
+    assert O.fp8_decode(O.fp8_encode(ties, O.KV_INT8), O.KV_INT8).tolist() == \
+        [0, 2, 2, 0, -2, 126, -128, 127, -128]
+    odd = np.array([np.nan, np.inf, -np.inf, 1e30, -1e30, -0.0], np.float32)
+    assert O.fp8_decode(O.fp8_encode(odd, O.KV_INT8), O.KV_INT8).tolist() == \
+        [0, 127, -128, 127, -128, 0]

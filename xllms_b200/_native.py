@@ -38,6 +38,7 @@ NXT_BT_GROUP_MEMBERS = 5
 NXT_BT_NUM_ARRAYS = 6
 NXT_KV_FP8_E4M3 = 1
 NXT_KV_FP8_E5M2 = 2
+NXT_KV_INT8 = 3
 NXT_ACT_SILU_AND_MUL = 0
 NXT_ACT_MUL_AND_SILU = 1
 NXT_ACT_GELU_AND_MUL = 2

@@ -18,6 +18,10 @@
 #include "pa_launch.h"
 #include "pa_prefix.h"
 
+static_assert(NXT_KV_FP8_E4M3 == xpa::kKvE4M3 && NXT_KV_FP8_E5M2 == xpa::kKvE5M2 &&
+                  NXT_KV_INT8 == xpa::kKvInt8,
+              "one-byte KV format codes");
+
 namespace {
 
 thread_local int g_last_error = NXT_PA_OK;
@@ -238,9 +242,9 @@ int prefix_chunk_pages(int max_prefix_pages) {
   return cp;
 }
 
-// Quantised KV cache of an fp8 call.
+// Quantised KV cache of a one-byte (fp8 / int8) call.
 struct KvQuant {
-  int fmt;  // xpa::kKvE4M3 or xpa::kKvE5M2
+  int fmt;  // xpa::kKvE4M3, xpa::kKvE5M2 or xpa::kKvInt8
   float k_scale, v_scale;
 };
 
@@ -264,7 +268,8 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   const int kv_fmt = kvq ? kvq->fmt : 0;
   const int kv_es = kvq ? 1 : ds;
   if (kvq) {
-    if ((kvq->fmt != xpa::kKvE4M3 && kvq->fmt != xpa::kKvE5M2) || ds != 2 ||
+    if ((kvq->fmt != xpa::kKvE4M3 && kvq->fmt != xpa::kKvE5M2 && kvq->fmt != xpa::kKvInt8) ||
+        ds != 2 ||
         !(kvq->k_scale > 0.f) || !(kvq->v_scale > 0.f) || !std::isfinite(kvq->k_scale) ||
         !std::isfinite(kvq->v_scale))
       return NXT_PA_EINVAL;
@@ -631,7 +636,8 @@ int nxt_reshape_and_cache_fp8(const void* key, const void* value, void* key_cach
   if (num_tokens < 0) return NXT_PA_EINVAL;
   if (num_tokens == 0) return NXT_PA_OK;
   if (!key || !value || !key_cache || !value_cache || !slot_mapping) return NXT_PA_EINVAL;
-  if ((kv_format != xpa::kKvE4M3 && kv_format != xpa::kKvE5M2) || !(k_scale > 0.f) ||
+  if ((kv_format != xpa::kKvE4M3 && kv_format != xpa::kKvE5M2 && kv_format != xpa::kKvInt8) ||
+      !(k_scale > 0.f) ||
       !(v_scale > 0.f) || !std::isfinite(k_scale) || !std::isfinite(v_scale))
     return NXT_PA_EINVAL;
   if (num_kv_heads <= 0 || head_size <= 0 || head_size > 256 || block_size <= 0 ||

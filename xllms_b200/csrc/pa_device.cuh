@@ -55,8 +55,8 @@ struct Params {
   // griddepcontrol.wait (the appended token lives there).
   int after_append;
   int join_primary;  // CTA 0 waits for the preceding grid before it exits
-  // Quantised KV cache: 0 = K/V in the query's dtype; kKvE4M3 / kKvE5M2 = one
-  // fp8 byte per element holding encode(x / scale). k_scale is folded into
+  // Quantised KV cache: 0 = K/V in the query's dtype; kKvE4M3 / kKvE5M2 /
+  // kKvInt8 = one byte per element holding encode(x / scale). k_scale is folded into
   // scale_log2; v_scale multiplies V (generic path) or O (fast path).
   int kv_fmt;
   float v_scale;
@@ -64,6 +64,7 @@ struct Params {
 
 constexpr int kKvE4M3 = 1;
 constexpr int kKvE5M2 = 2;
+constexpr int kKvInt8 = 3;  // two's-complement int8, decode(c) = c
 
 // KV append: token t's rows key/value[t*token_stride + h*D + d] go to the
 // pool slot slots[t] (page slot/block_size, slot slot%block_size).
@@ -76,9 +77,9 @@ struct AppendParams {
   long long kv_block_stride, kv_head_stride, token_stride;
   int num_tokens, Hkv, D, block_size;
   int vec16;  // every row 16-byte aligned: copy 16 bytes per lane
-  // fp8 cache (kKvE4M3 / kKvE5M2): the fp16 rows are stored as
-  // encode(x / k_scale) and encode(x / v_scale), rounded to nearest even and
-  // saturated at the format's largest finite value. 0: bit copy.
+  // one-byte cache (kKvE4M3 / kKvE5M2 / kKvInt8): the fp16 rows are stored
+  // as encode(x / k_scale) and encode(x / v_scale), rounded to nearest even
+  // and saturated at the format's largest finite value. 0: bit copy.
   int kv_fmt;
   float k_scale, v_scale;
 };
@@ -299,11 +300,21 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   return y;
 }
 
-// Two fp8 values (low byte first) -> fp16x2 (low half first); exact, since
-// every E4M3 and E5M2 value is an fp16 value.
+// Two one-byte codes (low byte first) -> fp16x2 (low half first); exact,
+// since every E4M3, E5M2 and int8 value is an fp16 value. int8: the byte
+// biased by 128 (c ^ 0x80 = c + 128 in 0..255) sits under the fp16 exponent
+// of 1024, where the spacing is 1, giving 1024 + 128 + c; subtracting 1152
+// is exact.
 template <int FMT>
 __device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t two) {
   uint32_t r;
+  if constexpr (FMT == kKvInt8) {
+    const uint32_t biased = __byte_perm(two ^ 0x8080u, 0x64646464u, 0x5140);
+    const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&biased),
+                              __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
+    r = *reinterpret_cast<const uint32_t*>(&h);
+    return r;
+  }
   const unsigned short v = (unsigned short)(two & 0xffffu);
   if constexpr (FMT == kKvE4M3)
     asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(v));
@@ -311,15 +322,40 @@ __device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t two) {
     asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(r) : "h"(v));
   return r;
 }
+// Four one-byte codes (byte 0 lowest) -> two fp16x2: lo = bytes 0, 1 and
+// hi = bytes 2, 3. int8 biases the whole word with one XOR.
+template <int FMT>
+__device__ __forceinline__ void kv8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  if constexpr (FMT == kKvInt8) {
+    const uint32_t x = w ^ 0x80808080u;
+    const uint32_t b0 = __byte_perm(x, 0x64646464u, 0x5140);
+    const uint32_t b1 = __byte_perm(x, 0x64646464u, 0x7362);
+    const __half2 off = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+    const __half2 h0 = __hsub2(*reinterpret_cast<const __half2*>(&b0), off);
+    const __half2 h1 = __hsub2(*reinterpret_cast<const __half2*>(&b1), off);
+    lo = *reinterpret_cast<const uint32_t*>(&h0);
+    hi = *reinterpret_cast<const uint32_t*>(&h1);
+  } else {
+    lo = fp8x2_to_h2<FMT>(w);
+    hi = fp8x2_to_h2<FMT>(w >> 16);
+  }
+}
 template <int FMT>
 __device__ __forceinline__ float fp8_to_float(uint8_t b) {
+  if constexpr (FMT == kKvInt8) return (float)(signed char)b;
   const uint32_t h2 = fp8x2_to_h2<FMT>(b);
   return __half2float(__ushort_as_half((unsigned short)(h2 & 0xffffu)));
 }
-// (a, b) -> two fp8 bytes, a in the low byte; round to nearest even,
-// saturating at the largest finite value (NaN stays NaN).
+// (a, b) -> two one-byte codes, a in the low byte; round to nearest even,
+// saturating at the largest finite value (fp8: NaN stays NaN; int8: the
+// range is [-128, 127] and NaN gives 0).
 template <int FMT>
 __device__ __forceinline__ uint32_t float2_to_fp8x2(float a, float b) {
+  if constexpr (FMT == kKvInt8) {
+    const int ia = min(max(__float2int_rn(a), -128), 127);
+    const int ib = min(max(__float2int_rn(b), -128), 127);
+    return ((uint32_t)ia & 0xffu) | (((uint32_t)ib & 0xffu) << 8);
+  }
   unsigned short r;
   // the first source operand lands in the upper byte
   if constexpr (FMT == kKvE4M3)

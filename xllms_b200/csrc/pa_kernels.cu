@@ -29,7 +29,8 @@ namespace xpa {
 // dimension (DPL dims per lane) and each token's K row is used for HG query
 // heads of the group at once, so K/V are read once per HG heads.
 // ════════════════════════════════════════════════════════════════════════
-// K/V element idx of a pool: T, or an fp8 byte (KVF = kKvE4M3 / kKvE5M2).
+// K/V element idx of a pool: T, or a one-byte code (KVF = kKvE4M3 / kKvE5M2 /
+// kKvInt8).
 template <typename T, int KVF>
 __device__ __forceinline__ float kv_load(const void* base, long long idx) {
   if constexpr (KVF == 0)
@@ -398,8 +399,9 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
         for (int nt = 0; nt < NT; ++nt) sc2[nt][0] = sc2[nt][1] = sc2[nt][2] = sc2[nt][3] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < C::kKSteps; ++ks) {
-          const uint32_t a0 = fp8x2_to_h2<KVF>(kw[ks][0]), a2 = fp8x2_to_h2<KVF>(kw[ks][0] >> 16);
-          const uint32_t a1 = fp8x2_to_h2<KVF>(kw[ks][1]), a3 = fp8x2_to_h2<KVF>(kw[ks][1] >> 16);
+          uint32_t a0, a1, a2, a3;
+          kv8x4_to_h2x2<KVF>(kw[ks][0], a0, a2);
+          kv8x4_to_h2x2<KVF>(kw[ks][1], a1, a3);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
             mma_f16_16816((ks & 1) ? sc2[nt] : sc[nt], a0, a1, a2, a3, qf[nt][ks][0],
@@ -444,10 +446,11 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
         for (int i = 0; i < ITER; ++i) {
           const int qi = lane + 32 * i, row = qi & 15, c8 = qi >> 4;
           const uint4 w = wv[i];
-          const uint32_t h0 = fp8x2_to_h2<KVF>(w.x), h1 = fp8x2_to_h2<KVF>(w.x >> 16);
-          const uint32_t h2 = fp8x2_to_h2<KVF>(w.y), h3 = fp8x2_to_h2<KVF>(w.y >> 16);
-          const uint32_t h4 = fp8x2_to_h2<KVF>(w.z), h5 = fp8x2_to_h2<KVF>(w.z >> 16);
-          const uint32_t h6 = fp8x2_to_h2<KVF>(w.w), h7 = fp8x2_to_h2<KVF>(w.w >> 16);
+          uint32_t h0, h1, h2, h3, h4, h5, h6, h7;
+          kv8x4_to_h2x2<KVF>(w.x, h0, h1);
+          kv8x4_to_h2x2<KVF>(w.y, h2, h3);
+          kv8x4_to_h2x2<KVF>(w.z, h4, h5);
+          kv8x4_to_h2x2<KVF>(w.w, h6, h7);
           const int chunk = 2 * c8;  // 8-element fp16 chunk of d = 16 c8
           asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(vsrc + tile_off(row, chunk)),
                        "r"(h0), "r"(h1), "r"(h2), "r"(h3)
@@ -633,10 +636,15 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
 #ifndef XPA_FP8_MIN_CTAS
 #define XPA_FP8_MIN_CTAS 5
 #endif
+#ifndef XPA_INT8_MIN_CTAS
+#define XPA_INT8_MIN_CTAS XPA_FP8_MIN_CTAS
+#endif
 template <int D, int NT, int STAGES, int NWC, int KVF>
 __global__ void __launch_bounds__((NWC + 1) * 32,
-                                  (D <= 128 && NT == 1) ? (KVF ? XPA_FP8_MIN_CTAS : XPA_FP16_MIN_CTAS)
-                                                        : 1)
+                                  (D <= 128 && NT == 1)
+                                      ? (KVF == kKvInt8 ? XPA_INT8_MIN_CTAS
+                                                        : KVF ? XPA_FP8_MIN_CTAS : XPA_FP16_MIN_CTAS)
+                                      : 1)
     pa_tma_mma_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const Params p) {
   tma_mma_body<D, NT, STAGES, NWC, KVF>(tmK, tmV, p);
@@ -753,7 +761,7 @@ __global__ void __launch_bounds__(128) pa_append_kernel(AppendParams a) {
   }
 }
 
-// KV append into an fp8 cache: fp16 rows in, encode(x / scale) bytes out
+// KV append into a one-byte cache: fp16 rows in, encode(x / scale) bytes out
 // (round to nearest even, saturating), 8 elements per lane and step when
 // every row is 16-byte (source) / 8-byte (cache) aligned.
 template <int KVF>
@@ -828,6 +836,8 @@ cudaError_t launch_generic_t(const Params& p, cudaStream_t st) {
       return launch_ex(pa_generic_kernel<T, DPL, HG, kKvE4M3>, (unsigned)grid, 128, 0, st, pdl, p);
     if (p.kv_fmt == kKvE5M2)
       return launch_ex(pa_generic_kernel<T, DPL, HG, kKvE5M2>, (unsigned)grid, 128, 0, st, pdl, p);
+    if (p.kv_fmt == kKvInt8)
+      return launch_ex(pa_generic_kernel<T, DPL, HG, kKvInt8>, (unsigned)grid, 128, 0, st, pdl, p);
   }
   return launch_ex(pa_generic_kernel<T, DPL, HG, 0>, (unsigned)grid, 128, 0, st, pdl, p);
 }
@@ -875,12 +885,21 @@ cudaError_t launch_generic_typed(const Params& p, cudaStream_t st) {
 #ifndef XPA_FP8_CONSUMER_WARPS
 #define XPA_FP8_CONSUMER_WARPS 2
 #endif
+// int8 caches: the same page rate as fp8, more conversion work per page.
+#ifndef XPA_INT8_RING_PAGES
+#define XPA_INT8_RING_PAGES XPA_FP8_RING_PAGES
+#endif
+#ifndef XPA_INT8_CONSUMER_WARPS
+#define XPA_INT8_CONSUMER_WARPS XPA_FP8_CONSUMER_WARPS
+#endif
 
 template <int D, int NT, int KVF>
 cudaError_t launch_fast_t(const CUtensorMap& tk, const CUtensorMap& tv, const Params& p,
                           cudaStream_t st) {
-  constexpr int RING = KVF ? XPA_FP8_RING_PAGES : XPA_RING_PAGES;
-  constexpr int NWC = KVF ? XPA_FP8_CONSUMER_WARPS : XPA_CONSUMER_WARPS;
+  constexpr int RING =
+      KVF == kKvInt8 ? XPA_INT8_RING_PAGES : KVF ? XPA_FP8_RING_PAGES : XPA_RING_PAGES;
+  constexpr int NWC = KVF == kKvInt8 ? XPA_INT8_CONSUMER_WARPS
+                                     : KVF ? XPA_FP8_CONSUMER_WARPS : XPA_CONSUMER_WARPS;
   // D = 256 pages are twice as large: half the ring, still a multiple of NWC
   constexpr int HALF = RING / 2 > NWC ? RING / 2 : NWC;
   constexpr int STAGES = (D == 256) ? (HALF + NWC - 1) / NWC * NWC : RING;
@@ -906,6 +925,7 @@ cudaError_t launch_fast_kv(const CUtensorMap& tk, const CUtensorMap& tv, const P
                            cudaStream_t st) {
   if (p.kv_fmt == kKvE4M3) return launch_fast_t<D, NT, kKvE4M3>(tk, tv, p, st);
   if (p.kv_fmt == kKvE5M2) return launch_fast_t<D, NT, kKvE5M2>(tk, tv, p, st);
+  if (p.kv_fmt == kKvInt8) return launch_fast_t<D, NT, kKvInt8>(tk, tv, p, st);
   return launch_fast_t<D, NT, 0>(tk, tv, p, st);
 }
 
@@ -919,7 +939,7 @@ cudaError_t launch_generic(const Params& p, int dtype_size, cudaStream_t st) {
 bool fast_path_shape_ok(int head_size, int group, int block_size, int dtype_size, int kv_fmt) {
   if (dtype_size != 2 || block_size != 16) return false;
   if (head_size != 64 && head_size != 128 && head_size != 256) return false;
-  if (kv_fmt != 0 && head_size == 64) return false;  // fp8 rows narrower than a 128-byte box
+  if (kv_fmt != 0 && head_size == 64) return false;  // 1-byte rows narrower than a 128-byte box
   if (group < 1 || group > 16) return false;
   if (group > 8 && head_size == 256) return false;  // accumulator registers
   return true;
@@ -963,6 +983,8 @@ cudaError_t launch_append(const AppendParams& a, int dtype_size, cudaStream_t st
     pa_append_fp8_kernel<kKvE4M3><<<grid, 128, 0, st>>>(a);
   else if (a.kv_fmt == kKvE5M2)
     pa_append_fp8_kernel<kKvE5M2><<<grid, 128, 0, st>>>(a);
+  else if (a.kv_fmt == kKvInt8)
+    pa_append_fp8_kernel<kKvInt8><<<grid, 128, 0, st>>>(a);
   else if (dtype_size == 4)
     pa_append_kernel<float><<<grid, 128, 0, st>>>(a);
   else

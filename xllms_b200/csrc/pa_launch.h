@@ -14,7 +14,7 @@ cudaError_t launch_generic(const Params& p, int dtype_size, cudaStream_t st);
 // TMA + tensor-core kernel; requires fast_path_shape_ok() and tensor maps
 // describing the K and V pools as {d, slot, kv head, page} with a 64 x 16 box
 // and 128-byte swizzle.
-// kv_fmt: 0 = K/V in the query's dtype, kKvE4M3 / kKvE5M2 = fp8 cache.
+// kv_fmt: 0 = K/V in the query's dtype, kKvE4M3 / kKvE5M2 / kKvInt8 = one-byte cache.
 bool fast_path_shape_ok(int head_size, int group, int block_size, int dtype_size, int kv_fmt = 0);
 cudaError_t launch_fast(const CUtensorMap& tk, const CUtensorMap& tv, const Params& p,
                         cudaStream_t st);

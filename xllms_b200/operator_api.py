@@ -405,8 +405,9 @@ def activation(name, x, *, out=None, stream=None):
     return out
 
 
-# ── fp8 KV cache ───────────────────────────────────────────────────────────
-FP8_FORMATS = {"e4m3": _native.NXT_KV_FP8_E4M3, "e5m2": _native.NXT_KV_FP8_E5M2}
+# ── one-byte KV cache (fp8 E4M3 / E5M2, int8) ──────────────────────────────
+FP8_FORMATS = {"e4m3": _native.NXT_KV_FP8_E4M3, "e5m2": _native.NXT_KV_FP8_E5M2,
+               "int8": _native.NXT_KV_INT8}
 
 
 def _fp8_code(fmt):
@@ -416,13 +417,14 @@ def _fp8_code(fmt):
 def paged_attention_fp8(query, key_cache, value_cache, block_tables, seq_lens, fmt, k_scale,
                         v_scale, *, scale=None, out=None, num_blocks=None, workspace=None,
                         device_status=None, stream=None):
-    """Decode attention over fp8 pools (uint8 tensors [NB, Hkv, P, D] holding
-    encode(x / scale)); query and output fp16 [B, Hq, D]."""
+    """Decode attention over one-byte pools (uint8 / int8 / float8 tensors
+    [NB, Hkv, P, D] holding encode(x / scale) in format `fmt`: "e4m3", "e5m2"
+    or "int8"); query and output fp16 [B, Hq, D]."""
     import torch
     B, Hq, D = query.shape
     nb, Hkv, bs, _ = key_cache.shape
     if key_cache.element_size() != 1 or value_cache.element_size() != 1:
-        raise PagedAttentionError(_native.NXT_PA_EINVAL, "fp8 pools must be 1-byte tensors")
+        raise PagedAttentionError(_native.NXT_PA_EINVAL, "one-byte pools must be 1-byte tensors")
     if out is None:
         out = torch.empty_like(query)
     if scale is None:
@@ -442,8 +444,9 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, seq_lens, f
 
 def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, fmt, k_scale, v_scale,
                           stream=None) -> None:
-    """Quantise fp16 key/value [T, Hkv, D] into the fp8 pools [NB, Hkv, P, D]
-    at slot_mapping[t] (int64; negative: skipped)."""
+    """Quantise fp16 key/value [T, Hkv, D] into the one-byte pools
+    [NB, Hkv, P, D] (format `fmt`) at slot_mapping[t] (int64; negative:
+    skipped)."""
     T, Hkv, D = key.shape
     nb, hk, bs, dk = key_cache.shape
     if (hk != Hkv or dk != D or tuple(value.shape) != tuple(key.shape)

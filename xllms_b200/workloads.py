@@ -148,12 +148,19 @@ class PagedBatch:
         return tuple(out)
 
     def values_torch_fp8(self, device, fmt: str = "e4m3"):
-        """Q (fp16) and K, V pools quantised to fp8 with one scale per pool
-        (max |x| maps to the format's largest value): (q, k8, v8, k_scale,
-        v_scale), the pools as uint8 tensors holding encode(x / scale)."""
+        """Q (fp16) and K, V pools quantised to one byte per element (fp8
+        "e4m3" / "e5m2", or "int8") with one scale per pool (max |x| maps to
+        the format's largest value): (q, k8, v8, k_scale, v_scale), the pools
+        as uint8 tensors holding encode(x / scale)."""
         import torch
         q, k, v = self.values_torch(device)
-        tdt, fmax = {"e4m3": (torch.float8_e4m3fn, 448.0), "e5m2": (torch.float8_e5m2, 57344.0)}[fmt]
+        tdt, fmax = {"e4m3": (torch.float8_e4m3fn, 448.0), "e5m2": (torch.float8_e5m2, 57344.0),
+                     "int8": (torch.int8, 127.0)}[fmt]
+
+        def enc(x):  # fp32 -> codes; int8 rounds half to even and saturates
+            if tdt is torch.int8:
+                return torch.nan_to_num(x, nan=0.0).round().clamp(-128, 127).to(torch.int8)
+            return x.to(tdt)
         out = [q]
         scales = []
         for pool in (k, v):
@@ -163,7 +170,7 @@ class PagedBatch:
             q8f = q8.view(-1)
             step = 1 << 27
             for i in range(0, flat.numel(), step):  # chunks bound the fp32 temporary
-                q8f[i:i + step] = (flat[i:i + step].float() / sc).to(tdt).view(torch.uint8)
+                q8f[i:i + step] = enc(flat[i:i + step].float() / sc).view(torch.uint8)
             out.append(q8)
             scales.append(sc)
             del pool
