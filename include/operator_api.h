@@ -285,6 +285,27 @@ int nxt_reshape_and_cache_fp8(
     int64_t kv_block_stride, int64_t kv_head_stride, int64_t token_stride,
     nxt_stream_t stream);
 
+/* Decode step on one-byte pools with the quantising append fused in:
+ * new_key/new_value (fp16 [num_seqs][num_kv_heads][head_size], one new token
+ * per sequence) are stored at slot_mapping[b] as nxt_reshape_and_cache_fp8
+ * stores them, then nxt_paged_attention_fp8_ex runs over seq_lens (which
+ * already count the new token) with the library's own workspace. The
+ * attention grid is a programmatic dependent of the append: only the load of
+ * each sequence's last page waits for it. */
+int nxt_paged_attention_fp8_append_ex(
+    void *out, const void *query,
+    void *key_cache, void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    const void *new_key, const void *new_value, const int64_t *slot_mapping,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq, int block_size,
+    int kv_format, float k_scale, float v_scale,
+    int64_t kv_block_stride, int64_t kv_head_stride,
+    int64_t num_blocks,
+    int *device_status,
+    nxt_stream_t stream);
+
 /* ── extension: block-table builder ─────────────────────────────────────
  * The glue between a continuous-batching scheduler and these kernels (the
  * reference's scheduler, src/core/scheduler.c:278-440, stops at the list of

@@ -127,3 +127,38 @@ def test_fp8_caller_workspace(cuda):
     with pytest.raises(PA.PagedAttentionError) as e:
         PA.paged_attention_fp8(*args, scale=b.scale, workspace=ws[:need - 1])
     assert e.value.code == _native.NXT_PA_EWORKSPACE
+
+
+@pytest.mark.parametrize("name,fmt,fmax", FMTS)
+@pytest.mark.parametrize("hq,d", [(32, 128), (16, 256), (8, 64)])
+def test_fp8_append_fused_decode_step(cuda, name, fmt, fmax, hq, d):
+    import torch
+    # lengths include the new token; 17, 33 and 2049 put it at slot 0 of a new page
+    lens = [1, 17, 33, 500, 2049, 5000]
+    hkv = 2
+    b = W.make_batch("f8ap", lens, hq, hkv, d, "f16", 62, value_std=0.5)
+    q, k8, v8, ks, vs = _quantised(b, fmt, fmax)
+    rng = np.random.default_rng(10)
+    new_k = (rng.standard_normal((b.num_seqs, hkv, d)) * 0.5).astype(np.float16)
+    new_v = (rng.standard_normal((b.num_seqs, hkv, d)) * 0.5).astype(np.float16)
+    slots = np.array([int(b.block_tables[i, (L - 1) // 16]) * 16 + (L - 1) % 16
+                      for i, L in enumerate(b.seq_lens)], dtype=np.int64)
+    # reference: quantise and scatter on the host, then attention over the codes
+    kr, vr = k8.copy(), v8.copy()
+    O.reshape_and_cache(O.fp8_encode(new_k.astype(np.float32) / np.float32(ks), fmt),
+                        O.fp8_encode(new_v.astype(np.float32) / np.float32(vs), fmt), kr, vr,
+                        slots, block_size=b.block_size)
+    ref = O.attention_fp8(q, kr, vr, fmt, ks, vs, b.block_tables, b.seq_lens, b.num_kv_heads,
+                          b.scale, f64=True)
+    kt, vt = torch.from_numpy(k8).to(cuda), torch.from_numpy(v8).to(cuda)
+    bt, sl = b.tables_torch(cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = PA.paged_attention_fp8_append(torch.from_numpy(q).to(cuda), kt, vt, bt, sl,
+                                        torch.from_numpy(new_k).to(cuda),
+                                        torch.from_numpy(new_v).to(cuda),
+                                        torch.from_numpy(slots).to(cuda), name, ks, vs,
+                                        scale=b.scale, device_status=status)
+    torch.cuda.synchronize()
+    check_close(out, ref, what=f"{name} fused append D={d}")
+    assert np.array_equal(kt.cpu().numpy(), kr) and np.array_equal(vt.cpu().numpy(), vr)
+    assert int(status.item()) == 0

@@ -86,3 +86,17 @@ def test_int8_codec():
     odd = np.array([np.nan, np.inf, -np.inf, 1e30, -1e30, -0.0], np.float32)
     assert O.fp8_decode(O.fp8_encode(odd, O.KV_INT8), O.KV_INT8).tolist() == \
         [0, 127, -128, 127, -128, 0]
+
+
+def test_fp8_append_step_argument_checks_without_gpu():
+    lib = _native.xpa()
+    buf = np.zeros(64, dtype=np.uint8)
+    p = buf.ctypes.data
+    bt = np.zeros(4, dtype=np.int32)
+    sl = np.ones(1, dtype=np.int32)
+    sm = np.zeros(1, dtype=np.int64)
+    args = lambda B, fmt, ks: (p, p, p, p, bt.ctypes.data, sl.ctypes.data, p, p, sm.ctypes.data,
+                               B, 1, 16, 1, 1.0, 1, 16, fmt, ks, 1.0, 256, 256, 1, None, None)
+    assert lib.nxt_paged_attention_fp8_append_ex(*args(1, 5, 1.0)) == _native.NXT_PA_EINVAL
+    assert lib.nxt_paged_attention_fp8_append_ex(*args(1, 3, 0.0)) == _native.NXT_PA_EINVAL
+    assert lib.nxt_paged_attention_fp8_append_ex(*args(0, 3, 1.0)) == _native.NXT_PA_OK

@@ -98,6 +98,11 @@ SIGNATURES = {
     "nxt_paged_attention_fp8_workspace_size": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "nxt_reshape_and_cache_fp8": (
         _I, [_CVP, _CVP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _F, _I64, _I64, _I64, _VP]),
+    "nxt_paged_attention_fp8_append_ex": (
+        _I,
+        [_VP, _CVP, _VP, _VP, _IP, _IP, _CVP, _CVP, _VP, _I, _I, _I, _I, _F, _I, _I, _I, _F, _F,
+         _I64, _I64, _I64, _VP, _VP],
+    ),
     "nxt_reshape_and_cache": (
         _I, [_CVP, _CVP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I64, _I64, _I64, _VP]),
     "nxt_paged_attention_append_ex": (

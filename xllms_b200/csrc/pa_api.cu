@@ -278,7 +278,8 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NXT_PA_ECUDA;
-  Plan pl = make_plan(B, Hq, D, Hkv, max_blocks, sm_count_of(dev), kv_es);
+  const int sms = sm_count_of(dev);
+  Plan pl = make_plan(B, Hq, D, Hkv, max_blocks, sms, kv_es);
   // A cascade call needs the TMA path's shapes; others run without the prefix
   // information, which gives the same result.
   CUtensorMap tk, tv;
@@ -303,30 +304,32 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
 
   int* status = dev_status;
   void* part = ws;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!status) {
-      DeviceState* d = nullptr;
-      rc = device_state_locked(dev, &d);
-      if (rc != NXT_PA_OK) return rc;
-      status = d->status;
-    }
-    if (pl.ws_bytes > 0) {
-      if (ws) {
-        if (ws_bytes < pl.ws_bytes) return NXT_PA_EWORKSPACE;
-      } else {
-        Workspace& w = g_ws[{dev, reinterpret_cast<uintptr_t>(st)}];
-        if (w.bytes < pl.ws_bytes) {
-          if (w.ptr) cudaFree(w.ptr);  // synchronises: no kernel still reads it
-          w.ptr = nullptr;
-          w.bytes = 0;
-          if (cudaMalloc(&w.ptr, pl.ws_bytes) != cudaSuccess) return NXT_PA_ENOMEM;
-          w.bytes = pl.ws_bytes;
-        }
-        part = w.ptr;
+  // A library-owned workspace stays locked until this call's kernels are
+  // enqueued: another host thread on the same stream could otherwise grow
+  // (free) it between the lookup and the launches. Nothing below takes g_mu.
+  std::unique_lock<std::mutex> lk(g_mu);
+  if (!status) {
+    DeviceState* d = nullptr;
+    rc = device_state_locked(dev, &d);
+    if (rc != NXT_PA_OK) return rc;
+    status = d->status;
+  }
+  if (pl.ws_bytes > 0) {
+    if (ws) {
+      if (ws_bytes < pl.ws_bytes) return NXT_PA_EWORKSPACE;
+    } else {
+      Workspace& w = g_ws[{dev, reinterpret_cast<uintptr_t>(st)}];
+      if (w.bytes < pl.ws_bytes) {
+        if (w.ptr) cudaFree(w.ptr);  // synchronises: no kernel still reads it
+        w.ptr = nullptr;
+        w.bytes = 0;
+        if (cudaMalloc(&w.ptr, pl.ws_bytes) != cudaSuccess) return NXT_PA_ENOMEM;
+        w.bytes = pl.ws_bytes;
       }
+      part = w.ptr;
     }
   }
+  if (part == ws) lk.unlock();  // caller-owned (or no) workspace
 
   xpa::Params p{};
   p.out = out;
@@ -387,7 +390,6 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
     pg.num_groups = pre->num_groups;
     pg.max_group_size = pre->max_group_size;
     pg.max_chunks = pchunks;
-    const int sms = sm_count_of(dev);
     if (xpa::prefix_tc_ok(p)) {
       // The persistent tcgen05 prefix kernel (compute-bound, one CTA per SM)
       // takes a few SMs; the suffix kernel, launched as its programmatic
@@ -668,6 +670,33 @@ int nxt_reshape_and_cache_fp8(const void* key, const void* value, void* key_cach
                 ? 1
                 : 0;
   return map_cuda(xpa::launch_append(a, 2, static_cast<cudaStream_t>(stream)));
+}
+
+int nxt_paged_attention_fp8_append_ex(void* out, const void* query, void* key_cache,
+                                      void* value_cache, const int* block_tables,
+                                      const int* seq_lens, const void* new_key,
+                                      const void* new_value, const int64_t* slot_mapping,
+                                      int num_seqs, int num_heads, int head_size,
+                                      int num_kv_heads, float scale, int max_num_blocks_per_seq,
+                                      int block_size, int kv_format, float k_scale,
+                                      float v_scale, int64_t kv_block_stride,
+                                      int64_t kv_head_stride, int64_t num_blocks,
+                                      int* device_status, nxt_stream_t stream) {
+  int rc = check_args(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs,
+                      num_heads, head_size, num_kv_heads, max_num_blocks_per_seq, block_size, 2,
+                      kv_block_stride, kv_head_stride);
+  if (rc != NXT_PA_OK || num_seqs == 0) return rc;
+  // format and scales are checked here, before anything is launched
+  rc = nxt_reshape_and_cache_fp8(new_key, new_value, key_cache, value_cache, slot_mapping,
+                                 num_seqs, num_kv_heads, head_size, block_size, kv_format,
+                                 k_scale, v_scale, kv_block_stride, kv_head_stride,
+                                 (int64_t)num_kv_heads * head_size, stream);
+  if (rc != NXT_PA_OK) return rc;
+  const KvQuant kq{kv_format, k_scale, v_scale};
+  return run(out, query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads,
+             head_size, num_kv_heads, scale, max_num_blocks_per_seq, block_size, 2,
+             kv_block_stride, kv_head_stride, num_blocks, nullptr, 0, device_status,
+             static_cast<cudaStream_t>(stream), nullptr, 0, true, nullptr, &kq);
 }
 
 int nxt_reshape_and_cache(const void* key, const void* value, void* key_cache, void* value_cache,

@@ -464,6 +464,36 @@ def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, fmt,
         raise PagedAttentionError(rc, "nxt_reshape_and_cache_fp8")
 
 
+def paged_attention_fp8_append(query, key_cache, value_cache, block_tables, seq_lens, new_key,
+                               new_value, slot_mapping, fmt, k_scale, v_scale, *, scale=None,
+                               out=None, num_blocks=None, device_status=None, stream=None):
+    """One decode step on one-byte pools with the quantising append fused in:
+    new_key/new_value (fp16 [B, Hkv, D]) are stored at slot_mapping[b] in
+    format `fmt` and included in the attention (seq_lens count them)."""
+    import torch
+    B, Hq, D = query.shape
+    nb, Hkv, bs, _ = key_cache.shape
+    if (tuple(value_cache.shape) != tuple(key_cache.shape)
+            or key_cache.element_size() != 1 or value_cache.element_size() != 1
+            or tuple(new_key.shape) != (B, Hkv, D) or tuple(new_value.shape) != (B, Hkv, D)
+            or not (new_key.is_contiguous() and new_value.is_contiguous())
+            or slot_mapping.numel() < B):
+        raise PagedAttentionError(_native.NXT_PA_EINVAL, "paged_attention_fp8_append: shapes")
+    if out is None:
+        out = torch.empty_like(query)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    rc = _native.xpa().nxt_paged_attention_fp8_append_ex(
+        _ptr(out), _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+        _ptr(seq_lens), _ptr(new_key), _ptr(new_value), _ptr(slot_mapping), B, Hq, D, Hkv,
+        float(scale), block_tables.shape[1], bs, _fp8_code(fmt), float(k_scale), float(v_scale),
+        Hkv * bs * D, bs * D, nb if num_blocks is None else int(num_blocks),
+        _ptr(device_status), _stream_ptr(stream))
+    if rc != _native.NXT_PA_OK:
+        raise PagedAttentionError(rc, "nxt_paged_attention_fp8_append_ex")
+    return out
+
+
 # ── block-table builder ────────────────────────────────────────────────────
 class BlockTables:
     """One decode step's kernel inputs on the device, built by
