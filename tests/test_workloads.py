@@ -79,3 +79,23 @@ def test_algorithmic_bytes_formula():
     bt = int(((L + 15) // 16).sum()) * 4
     assert b.algorithmic_bytes() == kv + qo + bt + 64 * 4
     assert b.flops() == int(L.sum()) * 32 * 4 * 128
+
+
+@pytest.mark.parametrize("cfg", ["c1", "c2", "c3", "c4", "c5"])
+def test_cpu_sample_fits_reference_offsets(cfg):
+    # The reference CPU attention forms page offsets as 32-bit int products
+    # (examples/run_gpt2.c:63); the bench's CPU sample keeps its pool inside.
+    import os
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    b = W.CONFIGS[cfg]()
+    seqs, lens = bench.sample_plan(b, 8)
+    assert seqs == list(range(len(seqs))) and 1 <= len(seqs) <= 8
+    pages = sum(-(-L // b.block_size) for L in lens)
+    per_page = b.block_size * b.num_heads * b.head_size
+    assert pages * per_page <= min(2**31 - 1, bench.REF_SAMPLE_ELEMS)
+    for s, L in zip(seqs, lens):
+        assert 0 < L <= int(b.seq_lens[s]) or (L == 0 and b.seq_lens[s] == 0)
+    if cfg == "c2":  # every sequence whole, as before the bound
+        assert len(seqs) == 8 and lens == [int(x) for x in b.seq_lens[:8]]
