@@ -147,3 +147,33 @@ def test_shard_descriptor_layout():
     from xllms_b200 import sharding as S
     assert ctypes.sizeof(S.NxtPaShard) == 144
     assert S.NxtPaShard.peer_out.offset == 16 and S.NxtPaShard.peer_flags.offset == 80
+
+
+def test_python_wrappers_refuse_bad_tensors_on_the_host():
+    # Every check runs before a pointer reaches the C ABI (no GPU needed).
+    torch = pytest.importorskip("torch")
+    q = torch.zeros(2, 8, 64, dtype=torch.float16)
+    kc = torch.zeros(4, 2, 16, 64, dtype=torch.float16)
+    bt = torch.zeros(2, 4, dtype=torch.int32)
+    sl = torch.ones(2, dtype=torch.int32)
+    cases = [
+        lambda: PA.paged_attention(q, kc.float(), kc.float(), bt, sl),          # K/V dtype
+        lambda: PA.paged_attention(q, kc, kc, bt.long(), sl),                   # table dtype
+        lambda: PA.paged_attention(q, kc, kc, bt, sl.long()),                   # lens dtype
+        lambda: PA.paged_attention(q, kc, kc, bt[:1], sl),                      # too few rows
+        lambda: PA.paged_attention(q, kc, kc, bt, sl, out=q.float()),           # out dtype
+        lambda: PA.paged_attention(q.transpose(0, 1), kc, kc, bt, sl),          # layout
+        lambda: PA.paged_attention(q, kc, kc, bt, sl),                          # host tensors
+        lambda: PA.paged_attention_fp8(q.float(), kc.to(torch.uint8), kc.to(torch.uint8), bt,
+                                       sl, "int8", 1.0, 1.0),                   # query dtype
+        lambda: PA.paged_attention_fp8(q, kc, kc, bt, sl, "e4m3", 1.0, 1.0),    # 2-byte pools
+        lambda: PA.reshape_and_cache(q[:, :2], q[:, :2], kc, kc,
+                                     torch.zeros(2, dtype=torch.int32)),        # slot dtype
+        lambda: PA.reshape_and_cache_fp8(q[:, :2].float(), q[:, :2].float(), kc.to(torch.uint8),
+                                         kc.to(torch.uint8), torch.zeros(2, dtype=torch.int64),
+                                         "e4m3", 1.0, 1.0),                     # key dtype
+    ]
+    for i, call in enumerate(cases):
+        with pytest.raises(PA.PagedAttentionError) as ei:
+            call()
+        assert ei.value.code == _native.NXT_PA_EINVAL, i

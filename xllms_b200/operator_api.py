@@ -111,6 +111,44 @@ def _dtype_size(t) -> int:
     raise PagedAttentionError(_native.NXT_PA_EINVAL, f"dtype {t.dtype}")
 
 
+def _check_attention_inputs(where, query, key_cache, value_cache, block_tables, seq_lens, out,
+                            one_byte=False):
+    """Host checks before any pointer reaches the C ABI: ranks, shapes, dtypes,
+    contiguity and device. The kernels read raw pointers in the reference
+    layout, so a mismatch there would be misread, not reported."""
+    import torch
+
+    def bad(msg):
+        raise PagedAttentionError(_native.NXT_PA_EINVAL, f"{where}: {msg}")
+    if query.dim() != 3 or key_cache.dim() != 4:
+        bad("query must be [B, Hq, D] and the pools [num_blocks, Hkv, block_size, D]")
+    B, Hq, D = query.shape
+    if key_cache.shape[3] != D or tuple(value_cache.shape) != tuple(key_cache.shape):
+        bad("cache shapes")
+    if one_byte:
+        if query.dtype != torch.float16:
+            bad("query must be fp16")
+        if key_cache.element_size() != 1 or value_cache.element_size() != 1:
+            bad("one-byte pools must be 1-byte tensors")
+    else:
+        _dtype_size(query)
+        if key_cache.dtype != query.dtype or value_cache.dtype != query.dtype:
+            bad("the K/V pools must have the query's dtype")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.shape[0] < B:
+        bad("block_tables must be int32 [B, max_blocks]")
+    if seq_lens.dtype != torch.int32 or seq_lens.numel() < B:
+        bad("seq_lens must be int32 [B]")
+    ts = [query, key_cache, value_cache, block_tables, seq_lens]
+    if out is not None:
+        if tuple(out.shape) != tuple(query.shape) or out.dtype != query.dtype:
+            bad("out must have the query's shape and dtype")
+        ts.append(out)
+    if not all(t.is_contiguous() for t in ts):
+        bad("non-contiguous input")
+    if not all(t.is_cuda and t.device == query.device for t in ts):
+        bad("every tensor must be on the query's CUDA device")
+
+
 def paged_attention(query, key_cache, value_cache, block_tables, seq_lens, *,
                     scale: Optional[float] = None, out=None, num_blocks: Optional[int] = None,
                     workspace=None, device_status=None, stream=None):
@@ -123,12 +161,10 @@ def paged_attention(query, key_cache, value_cache, block_tables, seq_lens, *,
     key_cache.shape[0], which lets the kernels mask out-of-range pages.
     """
     import torch
+    _check_attention_inputs("paged_attention", query, key_cache, value_cache, block_tables,
+                            seq_lens, out)
     B, Hq, D = query.shape
-    nb, Hkv, bs, Dk = key_cache.shape
-    if Dk != D or tuple(value_cache.shape) != tuple(key_cache.shape):
-        raise PagedAttentionError(_native.NXT_PA_EINVAL, "paged_attention: cache shapes")
-    if not (key_cache.is_contiguous() and value_cache.is_contiguous() and query.is_contiguous()):
-        raise PagedAttentionError(_native.NXT_PA_EINVAL, "paged_attention: non-contiguous input")
+    nb, Hkv, bs, _ = key_cache.shape
     if out is None:
         out = torch.empty_like(query)
     ds = _dtype_size(query)
@@ -256,6 +292,13 @@ def make_input(query, key_cache, value_cache, block_tables, seq_lens, scale=None
 
 
 # ── KV append ─────────────────────────────────────────────────────────────
+def _index_ok(slot_mapping, n, like) -> bool:
+    """slot_mapping: contiguous int64 with >= n entries on `like`'s device."""
+    import torch
+    return (slot_mapping.dtype == torch.int64 and slot_mapping.is_contiguous()
+            and slot_mapping.numel() >= n and slot_mapping.device == like.device)
+
+
 def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, stream=None) -> None:
     """Scatter key/value [T, Hkv, D] into the pools [NB, Hkv, P, D] at
     slot_mapping[t] (int64; page = slot // P, slot % P; negative: skipped)."""
@@ -264,8 +307,11 @@ def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, stream=N
     if (hk != Hkv or dk != D or tuple(value.shape) != tuple(key.shape)
             or tuple(value_cache.shape) != tuple(key_cache.shape)
             or not (key_cache.is_contiguous() and value_cache.is_contiguous())
-            or key.stride(1) != D or value.stride() != key.stride()
-            or slot_mapping.numel() < T):
+            or key.stride(2) != 1 or key.stride(1) != D or value.stride() != key.stride()
+            or key.dtype != key_cache.dtype or value.dtype != key_cache.dtype
+            or value_cache.dtype != key_cache.dtype
+            or not _index_ok(slot_mapping, T, key) or not key.is_cuda
+            or len({t.device for t in (key, value, key_cache, value_cache)}) != 1):
         raise PagedAttentionError(_native.NXT_PA_EINVAL, "reshape_and_cache: shapes")
     rc = _native.xpa().nxt_reshape_and_cache(
         _ptr(key), _ptr(value), _ptr(key_cache), _ptr(value_cache), _ptr(slot_mapping), T, Hkv, D,
@@ -281,12 +327,15 @@ def paged_attention_append(query, key_cache, value_cache, block_tables, seq_lens
     [B, Hkv, D] are written at slot_mapping[b] and included in the attention
     (seq_lens count them)."""
     import torch
+    _check_attention_inputs("paged_attention_append", query, key_cache, value_cache,
+                            block_tables, seq_lens, out)
     B, Hq, D = query.shape
     nb, Hkv, bs, _ = key_cache.shape
-    if (tuple(value_cache.shape) != tuple(key_cache.shape)
-            or tuple(new_key.shape) != (B, Hkv, D) or tuple(new_value.shape) != (B, Hkv, D)
+    if (tuple(new_key.shape) != (B, Hkv, D) or tuple(new_value.shape) != (B, Hkv, D)
+            or new_key.dtype != query.dtype or new_value.dtype != query.dtype
             or not (new_key.is_contiguous() and new_value.is_contiguous())
-            or slot_mapping.numel() < B):
+            or not _index_ok(slot_mapping, B, query) or new_key.device != query.device
+            or new_value.device != query.device):
         raise PagedAttentionError(_native.NXT_PA_EINVAL, "paged_attention_append: shapes")
     if out is None:
         out = torch.empty_like(query)
@@ -350,6 +399,8 @@ def paged_attention_prefix(query, key_cache, value_cache, block_tables, seq_lens
     every member's seq_len covers its prefix and its block-table row starts
     with the group's shared pages. The result equals paged_attention's."""
     import torch
+    _check_attention_inputs("paged_attention_prefix", query, key_cache, value_cache,
+                            block_tables, seq_lens, out)
     B, Hq, D = query.shape
     nb, Hkv, bs, _ = key_cache.shape
     if not isinstance(groups, PrefixGroups):
@@ -421,10 +472,10 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, seq_lens, f
     [NB, Hkv, P, D] holding encode(x / scale) in format `fmt`: "e4m3", "e5m2"
     or "int8"); query and output fp16 [B, Hq, D]."""
     import torch
+    _check_attention_inputs("paged_attention_fp8", query, key_cache, value_cache, block_tables,
+                            seq_lens, out, one_byte=True)
     B, Hq, D = query.shape
     nb, Hkv, bs, _ = key_cache.shape
-    if key_cache.element_size() != 1 or value_cache.element_size() != 1:
-        raise PagedAttentionError(_native.NXT_PA_EINVAL, "one-byte pools must be 1-byte tensors")
     if out is None:
         out = torch.empty_like(query)
     if scale is None:
@@ -447,14 +498,17 @@ def reshape_and_cache_fp8(key, value, key_cache, value_cache, slot_mapping, fmt,
     """Quantise fp16 key/value [T, Hkv, D] into the one-byte pools
     [NB, Hkv, P, D] (format `fmt`) at slot_mapping[t] (int64; negative:
     skipped)."""
+    import torch
     T, Hkv, D = key.shape
     nb, hk, bs, dk = key_cache.shape
     if (hk != Hkv or dk != D or tuple(value.shape) != tuple(key.shape)
             or tuple(value_cache.shape) != tuple(key_cache.shape)
             or key_cache.element_size() != 1 or value_cache.element_size() != 1
             or not (key_cache.is_contiguous() and value_cache.is_contiguous())
-            or key.stride(1) != D or value.stride() != key.stride()
-            or slot_mapping.numel() < T):
+            or key.stride(2) != 1 or key.stride(1) != D or value.stride() != key.stride()
+            or key.dtype != torch.float16 or value.dtype != torch.float16
+            or not _index_ok(slot_mapping, T, key) or not key.is_cuda
+            or len({t.device for t in (key, value, key_cache, value_cache)}) != 1):
         raise PagedAttentionError(_native.NXT_PA_EINVAL, "reshape_and_cache_fp8: shapes")
     rc = _native.xpa().nxt_reshape_and_cache_fp8(
         _ptr(key), _ptr(value), _ptr(key_cache), _ptr(value_cache), _ptr(slot_mapping), T, Hkv, D,
@@ -471,13 +525,15 @@ def paged_attention_fp8_append(query, key_cache, value_cache, block_tables, seq_
     new_key/new_value (fp16 [B, Hkv, D]) are stored at slot_mapping[b] in
     format `fmt` and included in the attention (seq_lens count them)."""
     import torch
+    _check_attention_inputs("paged_attention_fp8_append", query, key_cache, value_cache,
+                            block_tables, seq_lens, out, one_byte=True)
     B, Hq, D = query.shape
     nb, Hkv, bs, _ = key_cache.shape
-    if (tuple(value_cache.shape) != tuple(key_cache.shape)
-            or key_cache.element_size() != 1 or value_cache.element_size() != 1
-            or tuple(new_key.shape) != (B, Hkv, D) or tuple(new_value.shape) != (B, Hkv, D)
+    if (tuple(new_key.shape) != (B, Hkv, D) or tuple(new_value.shape) != (B, Hkv, D)
+            or new_key.dtype != torch.float16 or new_value.dtype != torch.float16
             or not (new_key.is_contiguous() and new_value.is_contiguous())
-            or slot_mapping.numel() < B):
+            or not _index_ok(slot_mapping, B, query) or new_key.device != query.device
+            or new_value.device != query.device):
         raise PagedAttentionError(_native.NXT_PA_EINVAL, "paged_attention_fp8_append: shapes")
     if out is None:
         out = torch.empty_like(query)
