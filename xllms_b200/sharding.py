@@ -155,10 +155,19 @@ class FusedHeadGather:
     def run(self, query, key_cache, value_cache, block_tables, seq_lens, scale, num_blocks,
             device_status=None, stream=None):
         from . import _native
-        from .operator_api import _ptr, _stream_ptr
-        self.step += 1
+        from .operator_api import _check_attention_inputs, _dtype_size, _ptr, _stream_ptr
+        _check_attention_inputs("FusedHeadGather.run", query, key_cache, value_cache,
+                                block_tables, seq_lens, None)
         B, Hq, D = query.shape
         nb, Hkv, bs, _ = key_cache.shape
+        # the peer buffers were sized for these: anything larger would be
+        # stored past their end on another GPU
+        if (B != self.B or Hq != self.H // self.world or D != self.D
+                or _dtype_size(query) != self.es):
+            raise ValueError(f"FusedHeadGather.run: batch [{B}, {Hq}, {D}] x {query.dtype} does "
+                             f"not match the buffers' [{self.B}, {self.H // self.world}, {self.D}]"
+                             f" x {self.es}-byte elements")
+        self.step += 1
         rc = self.lib.nxt_paged_attention_sharded(
             ctypes.byref(self.shard), self.step, _ptr(query), _ptr(key_cache), _ptr(value_cache),
             _ptr(block_tables), _ptr(seq_lens), B, Hq, D, Hkv, float(scale),
