@@ -340,6 +340,25 @@ __device__ __forceinline__ void kv8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t
     hi = fp8x2_to_h2<FMT>(w >> 16);
   }
 }
+// Four one-byte codes -> the fp16x2 pairs (byte 0, byte 2) and (byte 1,
+// byte 3), low half first.
+template <int FMT>
+__device__ __forceinline__ void kv8x4_to_h2_even_odd(uint32_t w, uint32_t& even, uint32_t& odd) {
+  if constexpr (FMT == kKvInt8) {
+    const uint32_t x = w ^ 0x80808080u;
+    const uint32_t b0 = __byte_perm(x, 0x64646464u, 0x4240);
+    const uint32_t b1 = __byte_perm(x, 0x64646464u, 0x4341);
+    const __half2 off = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+    const __half2 h0 = __hsub2(*reinterpret_cast<const __half2*>(&b0), off);
+    const __half2 h1 = __hsub2(*reinterpret_cast<const __half2*>(&b1), off);
+    even = *reinterpret_cast<const uint32_t*>(&h0);
+    odd = *reinterpret_cast<const uint32_t*>(&h1);
+  } else {
+    const uint32_t t = __byte_perm(w, 0u, 0x3120);  // bytes 0, 2 | 1, 3
+    even = fp8x2_to_h2<FMT>(t);
+    odd = fp8x2_to_h2<FMT>(t >> 16);
+  }
+}
 template <int FMT>
 __device__ __forceinline__ float fp8_to_float(uint8_t b) {
   if constexpr (FMT == kKvInt8) return (float)(signed char)b;

@@ -200,6 +200,15 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
 // Bound on the producer's wait for its own in-flight copies after a timeout.
 constexpr uint64_t kDrainBudgetNs = 1000000000ull;
 
+// One-byte pages: PV reads V's A fragments from registers loaded straight
+// from the ring stage (transposed 16-bit ldmatrix over the byte rows) before
+// the softmax, so the stage goes back to its producer at once and no fp16 V
+// tile is needed. 0 widens V into a per-warp fp16 tile instead (measured
+// slower on B200); a build may choose either for tuning sweeps.
+#ifndef XPA_KV8_DIRECT_V
+#define XPA_KV8_DIRECT_V 1
+#endif
+
 template <int D, int NT, int STAGES, int NWC, int KVF>
 struct FastCfg {
   static constexpr int kElem = KVF ? 1 : 2;      // bytes per K / V element
@@ -209,8 +218,10 @@ struct FastCfg {
   static constexpr int kBoxes = D * kElem / 128; // 128-byte-wide TMA boxes per row
   static constexpr int kBoxElems = 128 / kElem;
   static constexpr int kRing = STAGES * kStage;
-  // fp8 caches: each consumer warp widens its V page to an fp16 tile here
-  static constexpr int kV16 = KVF ? NWC * 16 * D * 2 : 0;
+  static constexpr bool kDirectV = KVF != 0 && XPA_KV8_DIRECT_V;
+  // one-byte caches without direct V: each consumer warp widens its V page
+  // to an fp16 tile here
+  static constexpr int kV16 = (KVF && !kDirectV) ? NWC * 16 * D * 2 : 0;
   static constexpr int kMerge = NWC * NT * 8 * (D + 4) * 4 + NWC * NT * 8 * 8;
   static constexpr int kBarOff = kRing + kV16 > kMerge ? kRing + kV16 : kMerge;
   static constexpr int kSmem = 1024 + kBarOff + STAGES * 16 + STAGES * 4;
@@ -422,11 +433,35 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
         }
       }
 
-      // fp8 cache: widen the V page into this warp's fp16 tile (rows >=
-      // ntok as zeros), in the fp16 tile layout the PV loads below expect;
-      // the ring stage is then free for the producer.
+      // One-byte cache: V's PV fragments come straight from the stage into
+      // registers (direct V, the default), or the V page is widened into this
+      // warp's fp16 tile (rows >= ntok as zeros) in the layout the fp16 PV
+      // loads expect. Either way the ring stage is then free for the producer.
       uint32_t vsrc = tv;
-      if constexpr (KVF != 0) {
+      // direct V: vr[x][h] holds, for d-block x (16 d) and tokens 8h..8h+7,
+      // lane (g, c)'s bytes V[8h + 2c][16x + 2g, +1], V[8h + 2c + 1][16x + 2g, +1]
+      uint32_t vr[C::kDirectV ? C::kKSteps : 1][2];
+      if constexpr (C::kDirectV) {
+        const int t = ((mi & 1) << 3) + r8;  // lanes 8q..8q+7: rows of matrix q
+#pragma unroll
+        for (int x = 0; x < C::kKSteps; x += 2) {
+          const int db = x + (mi >> 1);
+          ldsm_x4_trans(tv + (db >> 3) * 2048 + t * 128 + (((db & 7) ^ (t & 7)) << 4), vr[x][0],
+                        vr[x][1], vr[x + 1][0], vr[x + 1][1]);
+        }
+        if (ntok < 16) {  // slots past the sequence end: zero bytes (decode to 0)
+          const uint32_t m0 = (2 * c < ntok ? 0xffffu : 0u) | (2 * c + 1 < ntok ? 0xffff0000u : 0u);
+          const uint32_t m1 =
+              (2 * c + 8 < ntok ? 0xffffu : 0u) | (2 * c + 9 < ntok ? 0xffff0000u : 0u);
+#pragma unroll
+          for (int x = 0; x < C::kKSteps; ++x) {
+            vr[x][0] &= m0;
+            vr[x][1] &= m1;
+          }
+        }
+        __syncwarp();  // every lane's ring loads precede the release
+        if (lane == 0) mbar_arrive(bar_empty + 8 * s);
+      } else if constexpr (KVF != 0) {
         vsrc = sbase + C::kRing + warp * (16 * D * 2);
         constexpr int CH8 = D / 16;  // 16-byte fp8 chunks per row
         // lanes of one 8-lane store phase take 8 rows of one chunk column:
@@ -522,7 +557,14 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
 #pragma unroll
       for (int mt = 0; mt < C::kKSteps; ++mt) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4_trans(vsrc + tile_off(r8 + ((mi >> 1) << 3), 2 * mt + (mi & 1)), a0, a1, a2, a3);
+        if constexpr (C::kDirectV) {
+          // A rows of m-tile mt: g -> d = 16 mt + 2g, g + 8 -> d = 16 mt + 2g + 1
+          kv8x4_to_h2_even_odd<KVF>(vr[mt][0], a0, a1);
+          kv8x4_to_h2_even_odd<KVF>(vr[mt][1], a2, a3);
+        } else {
+          ldsm_x4_trans(vsrc + tile_off(r8 + ((mi >> 1) << 3), 2 * mt + (mi & 1)), a0, a1, a2,
+                        a3);
+        }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           mma_f16_16816(o[nt][mt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
@@ -560,8 +602,13 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
         float* row = sm_o + (warp * GS + head) * RS;
 #pragma unroll
         for (int mt = 0; mt < C::kKSteps; ++mt) {
-          row[mt * 16 + g] = o[nt][mt][k];
-          row[mt * 16 + g + 8] = o[nt][mt][2 + k];
+          if constexpr (C::kDirectV) {  // O^T rows are d = 16 mt + 2g, + 1
+            row[mt * 16 + 2 * g] = o[nt][mt][k];
+            row[mt * 16 + 2 * g + 1] = o[nt][mt][2 + k];
+          } else {
+            row[mt * 16 + g] = o[nt][mt][k];
+            row[mt * 16 + g + 8] = o[nt][mt][2 + k];
+          }
         }
         if (g == 0) {
           sm_ml[(warp * GS + head) * 2] = mrun[nt][k];
