@@ -675,13 +675,14 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
 
 // Resident CTAs per SM the register allocation must allow, for D <= 128 with
 // one 8-head tile: 6 for fp16 pages (the shared-memory limit of the 4-page
-// ring), 5 for fp8 pages. The wider variants (D = 256, 16 heads per KV head)
-// keep their registers instead: a bound would spill them.
+// ring), 4 for one-byte pages (3 consumer warps, 128 registers, 50 KB of ring
+// each). The wider variants (D = 256, 16 heads per KV head) keep their
+// registers instead: a bound would spill them.
 #ifndef XPA_FP16_MIN_CTAS
 #define XPA_FP16_MIN_CTAS 6
 #endif
 #ifndef XPA_FP8_MIN_CTAS
-#define XPA_FP8_MIN_CTAS 5
+#define XPA_FP8_MIN_CTAS 4
 #endif
 #ifndef XPA_INT8_MIN_CTAS
 #define XPA_INT8_MIN_CTAS XPA_FP8_MIN_CTAS
@@ -925,12 +926,14 @@ cudaError_t launch_generic_typed(const Params& p, cudaStream_t st) {
 #define XPA_CONSUMER_WARPS 2
 #endif
 
-// fp8 caches: pages are half the bytes, so a CTA needs twice the page rate.
+// One-byte caches: pages are half the bytes, so the SM needs twice the page
+// rate. With V read straight into registers (no fp16 V tiles), 3 consumer
+// warps sharing a 12-page ring, 4 CTAs per SM, measured fastest on B200.
 #ifndef XPA_FP8_RING_PAGES
-#define XPA_FP8_RING_PAGES 8
+#define XPA_FP8_RING_PAGES 12
 #endif
 #ifndef XPA_FP8_CONSUMER_WARPS
-#define XPA_FP8_CONSUMER_WARPS 2
+#define XPA_FP8_CONSUMER_WARPS 3
 #endif
 // int8 caches: the same page rate as fp8, more conversion work per page.
 #ifndef XPA_INT8_RING_PAGES
