@@ -233,12 +233,23 @@ int prefix_ctas(int B, int Hq, int D, int Hkv, int max_blocks, int num_groups,
   return std::min(sm_count, std::max(8, n));
 }
 
-// Pages per prefix partial slot: short chunks, so the prefix kernel (one CTA
-// per chunk x block of query rows x KV head) has enough CTAs; at most 64
-// chunks while a chunk stays within the kernel's 512 pages.
-int prefix_chunk_pages(int max_prefix_pages) {
-  int cp = 16;
+// Pages per prefix partial slot. The floor, which the workspace query sizes
+// for: short chunks (at most 64, each within the prefix kernel's 512 pages),
+// so the prefix kernel has items enough. Given the items one chunk index
+// yields (`items_per_chunk`: groups x KV heads x 128-row query blocks) and the
+// prefix grid (`ctas`), a call then takes chunks twice as long while the grid
+// keeps at least one item per CTA: fewer partial slots for the merge to read
+// (config 4 on B200: 16-page chunks 0.1177 ms, 32: 0.1118, 64: 0.1105,
+// 128: 0.1089).
+#ifndef XPA_PREFIX_CHUNK_PAGES
+#define XPA_PREFIX_CHUNK_PAGES 16
+#endif
+int prefix_chunk_pages(int max_prefix_pages, long long items_per_chunk = 0, int ctas = 0) {
+  int cp = XPA_PREFIX_CHUNK_PAGES;
   while (ceil_div(max_prefix_pages, cp) > 64 && cp < 512) cp <<= 1;
+  while (items_per_chunk > 0 && cp < 512 && cp < max_prefix_pages &&
+         items_per_chunk * ceil_div(max_prefix_pages, 2 * cp) >= ctas)
+    cp <<= 1;
   return cp;
 }
 
@@ -294,7 +305,15 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   int slots = pl.max_parts, pchunk = 1, pchunks = 0;
   if (pre) {
     if (!pre->prefix_pages || !pre->offsets || !pre->members) return NXT_PA_EINVAL;
-    pchunk = prefix_chunk_pages(pre->max_prefix_pages);
+    // longer chunks only for the tcgen05 prefix kernel (head sizes 64, 128)
+    const long long items_per_chunk =
+        (D == 64 || D == 128)
+            ? (long long)pre->num_groups * Hkv *
+                  ceil_div((long long)pre->max_group_size * (Hq / Hkv), 128)
+            : 0;
+    pchunk = prefix_chunk_pages(pre->max_prefix_pages, items_per_chunk,
+                                prefix_ctas(B, Hq, D, Hkv, max_blocks, pre->num_groups,
+                                            pre->max_group_size, pre->max_prefix_pages, sms));
     pchunks = ceil_div(pre->max_prefix_pages, pchunk);
     slots = pl.max_parts + pchunks;
     pl.ws_bytes = (size_t)B * Hq * slots * (size_t)(D + 2) * sizeof(float);
