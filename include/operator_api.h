@@ -426,7 +426,10 @@ int nxt_paged_attention_prefix_ex(
     int *device_status,
     nxt_stream_t stream);
 
-/* Workspace bytes a nxt_paged_attention_prefix_ex call with these sizes needs. */
+/* Workspace bytes that suffice for a nxt_paged_attention_prefix_ex call with
+ * these sizes: an upper bound, sized for the shortest prefix chunks (a call
+ * may take longer chunks, hence fewer partial slots, when its groups give the
+ * prefix kernel items enough). */
 size_t nxt_paged_attention_prefix_workspace_size(
     int num_seqs, int num_heads, int head_size, int num_kv_heads,
     int max_num_blocks_per_seq, int block_size, int max_prefix_pages);

@@ -109,3 +109,40 @@ def test_config4_cascade_matches_plain(cuda):
     q, k, v, bt2, sl2 = gather_subset(b, seqs, qt, kt, vt)
     ref = O.attention(q, k, v, bt2, sl2, b.num_kv_heads, b.scale)
     check_close(a[seqs], ref, what="cascade vs oracle")
+
+
+def test_config4_caller_workspace_of_the_queried_size(cuda):
+    """A caller workspace of exactly nxt_paged_attention_prefix_workspace_size
+    bytes serves a full-size config 4 cascade call (the query is an upper
+    bound of whatever prefix chunking the call picks), with the same result
+    as the library-owned workspace; a workspace far too small is refused."""
+    import torch
+    from xllms_b200 import _native
+    b = W.config4()
+    qt, kt, vt = b.values_torch(cuda)
+    bt, sl = b.tables_torch(cuda)
+    g = PA.PrefixGroups(b.prefix_groups, b.num_seqs, cuda)
+    lib = _native.xpa()
+    B, Hq, D, Hkv, bs = b.num_seqs, b.num_heads, b.head_size, b.num_kv_heads, b.block_size
+    need = lib.nxt_paged_attention_prefix_workspace_size(B, Hq, D, Hkv, b.max_blocks, bs,
+                                                         g.max_prefix_pages)
+    assert need > 0
+
+    def call(ws, nbytes):
+        out = torch.empty_like(qt)
+        rc = lib.nxt_paged_attention_prefix_ex(
+            out.data_ptr(), qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), bt.data_ptr(),
+            sl.data_ptr(), g.prefix_pages.data_ptr(), g.offsets.data_ptr(), g.members.data_ptr(),
+            g.num_groups, g.max_group_size, g.max_prefix_pages, B, Hq, D, Hkv, b.scale,
+            b.max_blocks, bs, 2, Hkv * bs * D, bs * D, b.num_blocks, ws, nbytes, None, None)
+        return rc, out
+
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda)
+    rc, out = call(ws.data_ptr(), need)
+    assert rc == _native.NXT_PA_OK
+    own = PA.paged_attention_prefix(qt, kt, vt, bt, sl, g, num_blocks=b.num_blocks)
+    torch.cuda.synchronize()
+    assert torch.equal(out, own)
+    assert PA.device_status() == 0
+    rc, _ = call(ws.data_ptr(), 1024)
+    assert rc == _native.NXT_PA_EWORKSPACE
