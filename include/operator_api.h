@@ -487,6 +487,24 @@ int nxt_paged_attention_sharded(
     int *device_status,
     nxt_stream_t stream);
 
+/* The same over one-byte pools: this rank's K/V pools as for
+ * nxt_paged_attention_fp8_ex (kv_format, k_scale, v_scale); query and the
+ * gathered output are fp16, so the gather buffers are sized with 2-byte
+ * elements. */
+int nxt_paged_attention_fp8_sharded(
+    const NxtPaShard *shard, uint64_t step,
+    const void *query,
+    const void *key_cache, const void *value_cache,
+    const int *block_tables, const int *seq_lens,
+    int num_seqs, int num_heads, int head_size,
+    int num_kv_heads, float scale,
+    int max_num_blocks_per_seq, int block_size,
+    int kv_format, float k_scale, float v_scale,
+    int64_t kv_block_stride, int64_t kv_head_stride,
+    int64_t num_blocks,
+    int *device_status,
+    nxt_stream_t stream);
+
 /* extension — instrumentation for timing the attention kernel alone. The next
  * call made by this host thread records `before` on its stream immediately
  * before the main attention kernel (before the shared-prefix kernel of a

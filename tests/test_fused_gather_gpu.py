@@ -124,3 +124,47 @@ def test_missing_peer_signal_times_out(cuda):
     assert int(status.item()) == 0
     for p in bufs:
         lib.nxt_pa_peer_free(p)
+
+
+@pytest.mark.parametrize("name,fmt,fmax", [("e4m3", O.FP8_E4M3, 448.0), ("int8", O.KV_INT8, 127.0)])
+def test_emulated_ranks_one_byte_pools(cuda, name, fmt, fmax):
+    """nxt_paged_attention_fp8_sharded: each emulated rank reads its heads'
+    one-byte pools and stores fp16 rows into both ranks' gather buffers; the
+    gathered output equals the oracle over the dequantised pools."""
+    import torch
+    lib = _native.xpa()
+    b = W.make_batch("fg8", [1, 700, 2100, 0, 5000, 16], 32, 8, 128, "f16", 83, value_std=0.5)
+    q, k, v = b.values_numpy()
+    ks = float(np.abs(k.astype(np.float32)).max()) / fmax
+    vs = float(np.abs(v.astype(np.float32)).max()) / fmax
+    k8 = O.fp8_encode(k.astype(np.float32) / np.float32(ks), fmt)
+    v8 = O.fp8_encode(v.astype(np.float32) / np.float32(vs), fmt)
+    ref = O.attention_fp8(q, k8, v8, fmt, ks, vs, b.block_tables, b.seq_lens, b.num_kv_heads,
+                          b.scale, f64=True)
+    bt, sl = b.tables_torch(cuda)
+    bufs, half, flags_off = _buffers(lib, b.num_seqs, 32, 128, 2, WORLD)
+    shards = _shards(bufs, flags_off, 32, WORLD)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    try:
+        for r in range(WORLD):
+            _flags(bufs[r] + flags_off, WORLD, cuda).fill_(1)
+        for r in range(WORLD):
+            qs, k8s, v8s = (torch.from_numpy(np.ascontiguousarray(x)).to(cuda) for x in
+                            S.shard_heads(q, k8, v8, b.num_kv_heads, WORLD, r))
+            rc = lib.nxt_paged_attention_fp8_sharded(
+                ctypes.byref(shards[r]), 1, qs.data_ptr(), k8s.data_ptr(), v8s.data_ptr(),
+                bt.data_ptr(), sl.data_ptr(), b.num_seqs, qs.shape[1], b.head_size,
+                k8s.shape[1], b.scale, b.max_blocks, 16, fmt, ks, vs,
+                k8s.shape[1] * 16 * b.head_size, 16 * b.head_size, b.num_blocks,
+                status.data_ptr(), None)
+            assert rc == 0
+            torch.cuda.synchronize()
+        for r in range(WORLD):
+            view = torch.as_tensor(S._DeviceArray(bufs[r] + half, (b.num_seqs, 32, 128), "<f2"),
+                                   device=cuda)
+            check_close(view, ref, what=f"{name} buffer {r}")
+        assert int(status.item()) == 0
+    finally:
+        torch.cuda.synchronize()
+        for p in bufs:
+            lib.nxt_pa_peer_free(p)

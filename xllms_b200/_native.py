@@ -119,6 +119,11 @@ SIGNATURES = {
         [_VP, ctypes.c_uint64, _CVP, _CVP, _CVP, _IP, _IP, _I, _I, _I, _I, _F, _I, _I, _I, _I64,
          _I64, _I64, _VP, _VP],
     ),
+    "nxt_paged_attention_fp8_sharded": (
+        _I,
+        [_VP, ctypes.c_uint64, _CVP, _CVP, _CVP, _IP, _IP, _I, _I, _I, _I, _F, _I, _I, _I, _F, _F,
+         _I64, _I64, _I64, _VP, _VP],
+    ),
     "nxt_paged_attention_set_wait_budget_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "nxt_paged_attention_device_info": (
         _I, [ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.c_char_p, _I]),

@@ -823,6 +823,22 @@ int nxt_paged_attention_sharded(const NxtPaShard* shard, uint64_t step, const vo
              static_cast<cudaStream_t>(stream), shard, step);
 }
 
+int nxt_paged_attention_fp8_sharded(const NxtPaShard* shard, uint64_t step, const void* query,
+                                    const void* key_cache, const void* value_cache,
+                                    const int* block_tables, const int* seq_lens, int num_seqs,
+                                    int num_heads, int head_size, int num_kv_heads, float scale,
+                                    int max_num_blocks_per_seq, int block_size, int kv_format,
+                                    float k_scale, float v_scale, int64_t kv_block_stride,
+                                    int64_t kv_head_stride, int64_t num_blocks,
+                                    int* device_status, nxt_stream_t stream) {
+  if (!shard) return NXT_PA_EINVAL;
+  const KvQuant kq{kv_format, k_scale, v_scale};
+  return run(nullptr, query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads,
+             head_size, num_kv_heads, scale, max_num_blocks_per_seq, block_size, 2,
+             kv_block_stride, kv_head_stride, num_blocks, nullptr, 0, device_status,
+             static_cast<cudaStream_t>(stream), shard, step, false, nullptr, &kq);
+}
+
 uint64_t nxt_paged_attention_set_wait_budget_ns(uint64_t budget_ns) {
   const uint64_t prev = g_wait_budget_ns;
   g_wait_budget_ns = budget_ns;

@@ -153,11 +153,15 @@ class FusedHeadGather:
         return self.views[step & 1]
 
     def run(self, query, key_cache, value_cache, block_tables, seq_lens, scale, num_blocks,
-            device_status=None, stream=None):
+            device_status=None, stream=None, kv_format=None, k_scale=1.0, v_scale=1.0):
+        """Enqueues the next step. With `kv_format` ("e4m3", "e5m2" or "int8")
+        the pools are one-byte pools holding encode(x / scale) and the query
+        is fp16 (nxt_paged_attention_fp8_sharded)."""
         from . import _native
-        from .operator_api import _check_attention_inputs, _dtype_size, _ptr, _stream_ptr
+        from .operator_api import (_check_attention_inputs, _dtype_size, _fp8_code, _ptr,
+                                   _stream_ptr)
         _check_attention_inputs("FusedHeadGather.run", query, key_cache, value_cache,
-                                block_tables, seq_lens, None)
+                                block_tables, seq_lens, None, one_byte=kv_format is not None)
         B, Hq, D = query.shape
         nb, Hkv, bs, _ = key_cache.shape
         # the peer buffers were sized for these: anything larger would be
@@ -168,13 +172,19 @@ class FusedHeadGather:
                              f"not match the buffers' [{self.B}, {self.H // self.world}, {self.D}]"
                              f" x {self.es}-byte elements")
         self.step += 1
-        rc = self.lib.nxt_paged_attention_sharded(
-            ctypes.byref(self.shard), self.step, _ptr(query), _ptr(key_cache), _ptr(value_cache),
-            _ptr(block_tables), _ptr(seq_lens), B, Hq, D, Hkv, float(scale),
-            block_tables.shape[1], bs, self.es, Hkv * bs * D, bs * D, int(num_blocks),
-            _ptr(device_status), _stream_ptr(stream))
+        head = (ctypes.byref(self.shard), self.step, _ptr(query), _ptr(key_cache),
+                _ptr(value_cache), _ptr(block_tables), _ptr(seq_lens), B, Hq, D, Hkv, float(scale),
+                block_tables.shape[1], bs)
+        tail = (Hkv * bs * D, bs * D, int(num_blocks), _ptr(device_status), _stream_ptr(stream))
+        if kv_format is None:
+            name = "nxt_paged_attention_sharded"
+            rc = self.lib.nxt_paged_attention_sharded(*head, self.es, *tail)
+        else:
+            name = "nxt_paged_attention_fp8_sharded"
+            rc = self.lib.nxt_paged_attention_fp8_sharded(*head, _fp8_code(kv_format),
+                                                         float(k_scale), float(v_scale), *tail)
         if rc != 0:
-            raise RuntimeError(f"nxt_paged_attention_sharded: {_native.strerror(rc)}")
+            raise RuntimeError(f"{name}: {_native.strerror(rc)}")
         return self.output(self.step)
 
     def close(self, barrier=None):
