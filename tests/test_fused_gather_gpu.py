@@ -168,3 +168,37 @@ def test_emulated_ranks_one_byte_pools(cuda, name, fmt, fmax):
         torch.cuda.synchronize()
         for p in bufs:
             lib.nxt_pa_peer_free(p)
+
+
+def test_fused_head_gather_class_one_rank(cuda):
+    """FusedHeadGather (the class bench.py drives at N > 1) with one rank:
+    fp16 pools, then fp8 pools through run(kv_format=...), each equal to the
+    oracle, and a batch larger than its buffers refused on the host."""
+    import torch
+    b = W.make_batch("fgc", [1, 700, 2100, 0, 5000, 16], 32, 8, 128, "f16", 84, value_std=0.5)
+    q, k, v = b.values_numpy()
+    bt, sl = b.tables_torch(cuda)
+    qt, kt, vt = (torch.from_numpy(x).to(cuda) for x in (q, k, v))
+    fg = S.FusedHeadGather(b.num_seqs, 32, 128, 2, 1, 0, lambda blob: [blob], cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    try:
+        out = fg.run(qt, kt, vt, bt, sl, b.scale, b.num_blocks, device_status=status)
+        torch.cuda.synchronize()
+        check_close(out, O.attention(q, k, v, b.block_tables, b.seq_lens, 8, b.scale),
+                    what="fp16 pools")
+        ks = float(np.abs(k.astype(np.float32)).max()) / 448.0
+        vs = float(np.abs(v.astype(np.float32)).max()) / 448.0
+        k8 = O.fp8_encode(k.astype(np.float32) / np.float32(ks), O.FP8_E4M3)
+        v8 = O.fp8_encode(v.astype(np.float32) / np.float32(vs), O.FP8_E4M3)
+        out = fg.run(qt, torch.from_numpy(k8).to(cuda), torch.from_numpy(v8).to(cuda), bt, sl,
+                     b.scale, b.num_blocks, device_status=status, kv_format="e4m3",
+                     k_scale=ks, v_scale=vs)
+        torch.cuda.synchronize()
+        check_close(out, O.attention_fp8(q, k8, v8, O.FP8_E4M3, ks, vs, b.block_tables,
+                                         b.seq_lens, 8, b.scale, f64=True), what="fp8 pools")
+        assert int(status.item()) == 0
+        with pytest.raises(ValueError):
+            fg.run(torch.cat([qt, qt]), kt, vt, torch.cat([bt, bt]), torch.cat([sl, sl]),
+                   b.scale, b.num_blocks)
+    finally:
+        fg.close()
