@@ -59,3 +59,39 @@ def gather_subset(batch: W.PagedBatch, seqs, q_t, k_t, v_t):
         bt[i, :len(r)] = r
     sl = batch.seq_lens[list(seqs)].astype(np.int32)
     return q, k, v, bt, sl
+
+
+def plant_hot_keys(b: W.PagedBatch, q, k, v, pick, encode):
+    """Index-logic fixture, modified in place: Q = 1 and K = 0 except one
+    hot key (8.0 in every dim) per (sequence, KV head) at token
+    pick(i, h, L); V rows hold encode(page, slot, kv_head), four integers
+    >= 1, in dims 0-3 and 0 elsewhere. The hot key's score is 8*sqrt(D)
+    nats above the rest, so its weight is 1 and every query head of the
+    group must return the hot cell's integers exactly. Returns those
+    expected rows [B, Hq, 4]."""
+    q[:] = 1
+    k[:] = 0
+    v[:] = 0
+    nb, hkv, bs, _ = k.shape
+    pages, heads, slots = np.meshgrid(np.arange(nb), np.arange(hkv), np.arange(bs),
+                                      indexing="ij")
+    for c, x in enumerate(encode(pages, slots, heads)):
+        v[..., c] = x
+    group = q.shape[1] // hkv
+    expect = np.zeros((b.num_seqs, q.shape[1], 4), dtype=np.float64)
+    for i, L in enumerate(int(x) for x in b.seq_lens):
+        if L == 0:
+            continue
+        for h in range(hkv):
+            t = pick(i, h, L)
+            page, slot = int(b.block_tables[i, t // bs]), t % bs
+            k[page, h, slot, :] = 8.0
+            expect[i, h * group:(h + 1) * group] = encode(page, slot, h)
+    return expect
+
+
+def assert_hot_cells(out, expect):
+    """Bit-exact check of plant_hot_keys' expected rows; dims >= 4 are 0."""
+    got = out.double().cpu().numpy() if hasattr(out, "cpu") else np.asarray(out, np.float64)
+    assert np.array_equal(got[:, :, :4], expect)
+    assert not np.any(got[:, :, 4:])

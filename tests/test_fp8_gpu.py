@@ -162,3 +162,36 @@ def test_fp8_append_fused_decode_step(cuda, name, fmt, fmax, hq, d):
     check_close(out, ref, what=f"{name} fused append D={d}")
     assert np.array_equal(kt.cpu().numpy(), kr) and np.array_equal(vt.cpu().numpy(), vr)
     assert int(status.item()) == 0
+
+
+@pytest.mark.parametrize("name,fmt,head_size", [("int8", O.KV_INT8, 128), ("int8", O.KV_INT8, 64),
+                                                ("e4m3", O.FP8_E4M3, 128)])
+def test_one_byte_index_logic_bit_exact(cuda, name, fmt, head_size):
+    """Indexing over one-byte pools, exact: plant_hot_keys with scale 1 and
+    cell integers the format holds exactly (int8: up to 127; E4M3: up to
+    16). D = 128 takes the TMA path, D = 64 the CUDA-core one."""
+    import torch
+    from _helpers import assert_hot_cells, plant_hot_keys
+    lens = [1, 15, 16, 17, 33, 511, 512, 513, 2000, 4097, 300, 64]
+    b = W.make_batch("idx8", lens, 8, 2, head_size, "f16", 92)
+    q, k, v = b.values_numpy()
+    rng = np.random.default_rng(7)
+
+    def pick(i, h, L):
+        picks = [L - 1, 0, 15, 16, L // 2, int(rng.integers(0, L))]
+        return min(picks[(2 * i + h) % len(picks)], L - 1)
+
+    if fmt == O.KV_INT8:
+        enc = lambda p, s, h: (p % 100 + 1, p // 100 + 1, s + 1, h + 1)
+    else:
+        enc = lambda p, s, h: (p % 16 + 1, (p // 16) % 16 + 1, s + 1, h + 1)
+    expect = plant_hot_keys(b, q, k, v, pick, enc)
+    k8 = O.fp8_encode(k.astype(np.float32), fmt)
+    v8 = O.fp8_encode(v.astype(np.float32), fmt)
+    assert np.array_equal(O.fp8_decode(v8, fmt), v.astype(np.float32))  # cells held exactly
+    bt, sl = b.tables_torch(cuda)
+    out = PA.paged_attention_fp8(torch.from_numpy(q).to(cuda), torch.from_numpy(k8).to(cuda),
+                                 torch.from_numpy(v8).to(cuda), bt, sl, name, 1.0, 1.0,
+                                 scale=b.scale, num_blocks=b.num_blocks)
+    assert PA.device_status() == 0
+    assert_hot_cells(out, expect)

@@ -2,7 +2,8 @@
 import numpy as np
 import pytest
 
-from _helpers import RTOL, check_close, gather_subset, oracle_out, to_device
+from _helpers import (RTOL, assert_hot_cells, check_close, gather_subset, oracle_out,
+                      plant_hot_keys, to_device)
 from oracle import oracle as O
 from xllms_b200 import _native
 from xllms_b200 import operator_api as PA
@@ -271,39 +272,21 @@ def test_full_size_configs_sampled(cuda, cfg):
     (128, "f16", 4, 32),   # CUDA-core path, 32-token pages
 ])
 def test_index_logic_bit_exact(cuda, head_size, dtype, group, block_size):
-    """Block-table and head indexing, checked exactly. Each (sequence, KV
-    head) gets one hot key whose score is 8*sqrt(D) nats above every other
-    token's 0, so its weight is 1. V rows hold their own (page % 1024,
-    page // 1024, slot, KV head) + 1 as small integers: every expected value
-    is >= 1, so the other tokens' e^-64 (or smaller) weights round away, and
-    every query head of the group must return exactly the hot token's cell.
-    Hot positions cover page edges and split partitions."""
+    """Block-table, slot and head indexing, checked by exact equality: one
+    hot key per (sequence, KV head), V rows encoding their own cell
+    (plant_hot_keys). Hot positions cover page edges and split partitions."""
     lens = [1, 15, 16, 17, 33, 511, 512, 513, 2000, 4097, 300, 64]
-    hkv = 2
-    b = W.make_batch("idx", lens, group * hkv, hkv, head_size, dtype, 91,
-                     block_size=block_size)
+    b = W.make_batch("idx", lens, group * 2, 2, head_size, dtype, 91, block_size=block_size)
     q, k, v = b.values_numpy()
-    q[:] = 1
-    k[:] = 0
-    v[:] = 0
-    pages = np.arange(k.shape[0])
-    v[:, :, :, 0] = (pages % 1024 + 1)[:, None, None]
-    v[:, :, :, 1] = (pages // 1024 + 1)[:, None, None]
-    v[:, :, :, 2] = np.arange(1, block_size + 1)[None, None, :]
-    v[:, :, :, 3] = np.arange(1, hkv + 1)[None, :, None]
     rng = np.random.default_rng(6)
-    expect = np.zeros((b.num_seqs, group * hkv, 4), dtype=np.float64)
-    for i, L in enumerate(int(x) for x in b.seq_lens):
+
+    def pick(i, h, L):
         picks = [L - 1, 0, block_size - 1, block_size, L // 2, int(rng.integers(0, L))]
-        for h in range(hkv):
-            t = min(picks[(2 * i + h) % len(picks)], L - 1)
-            page, slot = int(b.block_tables[i, t // block_size]), t % block_size
-            k[page, h, slot, :] = 8.0
-            expect[i, h * group:(h + 1) * group] = (page % 1024 + 1, page // 1024 + 1,
-                                                    slot + 1, h + 1)
+        return min(picks[(2 * i + h) % len(picks)], L - 1)
+
+    expect = plant_hot_keys(b, q, k, v, pick,
+                            lambda p, s, h: (p % 1024 + 1, p // 1024 + 1, s + 1, h + 1))
     qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
     out = PA.paged_attention(qt, kt, vt, bt, sl, num_blocks=b.num_blocks)
     assert PA.device_status() == 0
-    got = out.double().cpu().numpy()
-    assert np.array_equal(got[:, :, :4], expect)
-    assert not np.any(got[:, :, 4:])
+    assert_hot_cells(out, expect)

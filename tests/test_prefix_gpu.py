@@ -146,3 +146,30 @@ def test_config4_caller_workspace_of_the_queried_size(cuda):
     assert PA.device_status() == 0
     rc, _ = call(ws.data_ptr(), 1024)
     assert rc == _native.NXT_PA_EWORKSPACE
+
+
+def test_cascade_index_logic_bit_exact(cuda):
+    """Indexing through the cascade kernels, exact (plant_hot_keys): for KV
+    head 0 each group's hot key lies in its shared prefix (every member must
+    return that prefix cell), for KV head 1 in each member's private suffix;
+    plus sequences in no group."""
+    from _helpers import assert_hot_cells, plant_hot_keys
+    prefix, members = [2048, 512], [5, 3]
+    suffix = [1, 17, 300, 1000, 16, 40, 513, 2, 70, 900]
+    b = _batch(prefix, members, suffix, 8, 2, 128, 93, no_group=2)
+    prefix_of = [0] * 5 + [1] * 3 + [-1] * 2
+    q, k, v = b.values_numpy()
+
+    def pick(i, h, L):
+        g = prefix_of[i]
+        plen = prefix[g] if g >= 0 else 0
+        if h == 0 and g >= 0:
+            return (prefix[g] // 3) + 16 * g  # one position per group
+        return plen + (i * 37) % (L - plen)  # this sequence's private tokens
+
+    expect = plant_hot_keys(b, q, k, v, pick,
+                            lambda p, s, h: (p % 1024 + 1, p // 1024 + 1, s + 1, h + 1))
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = PA.paged_attention_prefix(qt, kt, vt, bt, sl, b.prefix_groups, num_blocks=b.num_blocks)
+    assert PA.device_status() == 0
+    assert_hot_cells(out, expect)
