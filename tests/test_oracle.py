@@ -177,3 +177,39 @@ def test_gather_checksum_matches_python():
                     continue
                 acc = (acc + lib.pa_gather_mix(phys, t % 16, h // g)) % (1 << 64)
             assert int(cs[s, h]) == acc
+
+
+@pytest.mark.parametrize("head_size,dtype,group,block_size,fmt", [
+    (128, "f16", 4, 16, 0), (64, "f32", 1, 16, 0), (128, "f16", 4, 32, 0),
+    (64, "f16", 4, 16, O.KV_INT8), (64, "f16", 4, 16, O.FP8_E4M3)])
+def test_oracle_index_logic_exact(head_size, dtype, group, block_size, fmt):
+    """The oracle returns each (sequence, KV head)'s hot cell exactly under
+    the GPU tests' hot-key fixture (plant_hot_keys), for plain and one-byte
+    pools: the fixture's expectation is exact for the fp32 restatement too."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from _helpers import plant_hot_keys
+    lens = [1, 15, 16, 17, 33, 511, 512, 513, 2000, 300, 64]
+    b = W.make_batch("idxo", lens, group * 2, 2, head_size, dtype, 94, block_size=block_size)
+    q, k, v = b.values_numpy()
+    rng = np.random.default_rng(8)
+
+    def pick(i, h, L):
+        picks = [L - 1, 0, block_size - 1, block_size, L // 2, int(rng.integers(0, L))]
+        return min(picks[(2 * i + h) % len(picks)], L - 1)
+
+    if fmt == O.FP8_E4M3:
+        enc = lambda p, s, h: (p % 16 + 1, (p // 16) % 16 + 1, s + 1, h + 1)
+    else:
+        enc = lambda p, s, h: (p % 100 + 1, p // 100 + 1, s + 1, h + 1)
+    expect = plant_hot_keys(b, q, k, v, pick, enc)
+    if fmt:
+        k8 = O.fp8_encode(k.astype(np.float32), fmt)
+        v8 = O.fp8_encode(v.astype(np.float32), fmt)
+        out = O.attention_fp8(q, k8, v8, fmt, 1.0, 1.0, b.block_tables, b.seq_lens, 2, b.scale,
+                              block_size=block_size)
+    else:
+        out = O.attention(q, k, v, b.block_tables, b.seq_lens, 2, b.scale, block_size=block_size)
+    out = np.asarray(out, dtype=np.float64)
+    assert np.array_equal(out[:, :, :4], expect)
+    assert not np.any(out[:, :, 4:])
