@@ -115,9 +115,12 @@ const char *nxt_paged_attention_strerror(int code);
  *   num_blocks        pages in each cache pool; > 0 lets the kernels mask
  *                     entries >= num_blocks, <= 0 means unknown.
  *   workspace         device memory for split-context partials, at least
- *                     nxt_paged_attention_workspace_size(...) bytes, or NULL
- *                     to use the library's per-(device, stream) workspace,
- *                     which is allocated on first use and grown as needed.
+ *                     nxt_paged_attention_workspace_size(...) bytes and
+ *                     starting on a 16-byte boundary (NXT_PA_EINVAL
+ *                     otherwise), or NULL to use the library's per-(device,
+ *                     stream) workspace, which is allocated on first use and
+ *                     grown as needed. The same rule holds for every _ex call
+ *                     that takes a workspace.
  *   device_status     device int the kernels OR their NXT_PA_DEV_* bits into,
  *                     or NULL for the library's per-device status word.
  * Returns NXT_PA_OK once the kernels are enqueued, else a negative code.
@@ -175,7 +178,12 @@ int nxt_paged_attention_release_workspaces(void);
  *     (nxt_paged_attention_workspace_size(...) > NXT_PA_NOALLOC_SCRATCH_BYTES)
  *     returns NXT_PA_ESCRATCH and launches nothing.
  *   - The first call on each device looks up the array's device address
- *     (set-up); make that first call before any stream capture.
+ *     (set-up); make that first call before any stream capture. The address
+ *     is kept for the life of the process: after cudaDeviceReset on a device
+ *     (which unloads the library's module there) this entry point must not
+ *     be called on that device again.
+ *   - Its kernels' pipeline waits follow nxt_paged_attention_set_wait_budget_ns
+ *     like every other call from the same host thread.
  *   - Every call shares the one array and leaves its partials there; calls
  *     whose kernels overlap on the GPU (other streams, other host threads on
  *     the same device) race on it. Nothing in it needs clearing between calls.

@@ -92,6 +92,58 @@ def test_invalid_arguments_rejected_before_any_launch(bad):
     assert ei.value.code == _native.NXT_PA_EINVAL
 
 
+def _plan_parts(B, Hkv, max_blocks, per_sm=12, nsm=148, part_pages=128):
+    """Partition count of one call: the library's planning rule restated
+    (partitions halve, down to 4 pages, while the grid holds fewer than
+    per_sm items per SM; the SM count is 148 when no device answers)."""
+    pp = part_pages
+    while pp > 4 and B * Hkv * -(-max_blocks // pp) < per_sm * nsm:
+        pp //= 2
+    while -(-max_blocks // pp) > 8192:
+        pp *= 2
+    return -(-max_blocks // pp)
+
+
+def _partial_bytes(rows_slots, D):
+    """part_o [rows][slots][D] fp32, then the (max, sum) pairs from the next
+    256-byte boundary."""
+    off = -(-(rows_slots * D * 4) // 256) * 256
+    return off + rows_slots * 8
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,mb", [(3, 3, 1, 33, 12), (3, 9, 3, 65, 313),
+                                           (1, 1, 1, 127, 12), (64, 32, 8, 128, 512)])
+def test_workspace_size_pads_the_pair_table_to_an_aligned_offset(B, Hq, Hkv, D, mb):
+    """Odd head size x odd query heads x odd partition count puts the end of
+    the partial outputs on a 4-byte boundary; the size queries must count the
+    padding that starts the (max, sum) pairs on a 256-byte boundary."""
+    parts = _plan_parts(B, Hkv, mb)
+    assert parts > 1
+    lib = _native.xpa()
+    got = lib.nxt_paged_attention_workspace_size(B, Hq, D, Hkv, mb, 16, 2)
+    assert got == _partial_bytes(B * Hq * parts, D)
+    parts8 = _plan_parts(B, Hkv, mb, per_sm=24)
+    assert lib.nxt_paged_attention_fp8_workspace_size(B, Hq, D, Hkv, mb, 16) == \
+        _partial_bytes(B * Hq * parts8, D)
+    # the cascade query adds the prefix chunks' slots (16-page chunks, the floor)
+    pre = 32
+    assert lib.nxt_paged_attention_prefix_workspace_size(B, Hq, D, Hkv, mb, 16, pre) == \
+        _partial_bytes(B * Hq * (parts + -(-pre // 16)), D)
+
+
+def test_misaligned_caller_workspace_rejected_before_any_launch():
+    """A caller workspace that does not start on a 16-byte boundary is refused
+    with NXT_PA_EINVAL before anything touches a device."""
+    lib = _native.xpa()
+    p = ctypes.c_void_p(4096)
+    ip = ctypes.cast(p, ctypes.POINTER(ctypes.c_int))
+    for ws in (4100, 4104, 4108):
+        rc = lib.nxt_paged_attention_ex(p, p, p, p, ip, ip, 3, 3, 33, 1, 0.17, 12, 16, 2,
+                                        16 * 33, 16 * 33, 64, ctypes.c_void_p(ws), 1 << 20,
+                                        None, None)
+        assert rc == _native.NXT_PA_EINVAL
+
+
 def test_strerror():
     for code in (0, -22, -12, -28, -5, 77):
         assert _native.strerror(code)

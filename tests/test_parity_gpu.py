@@ -86,6 +86,33 @@ def test_split_context(cuda, lens):
     check_close(out, ref, what=f"split {lens}")
 
 
+@pytest.mark.parametrize("head_size", [33, 65, 127])
+@pytest.mark.parametrize("dtype", ["f16", "f32"])
+def test_odd_head_sizes_split_context(cuda, head_size, dtype):
+    """Odd head size, odd query-head count and an odd partition count: the
+    partial outputs then end on a 4-byte boundary, and the (max, sum) pairs the
+    merge reads as 8-byte loads must still start aligned. Also through a
+    caller workspace of exactly the size the query reports."""
+    import torch
+    b = W.make_batch("odd", [5000, 3, 2049], 3, 1, head_size, dtype, 61 + head_size)
+    need = PA.workspace_size(b.num_seqs, b.num_heads, head_size, 1, b.max_blocks,
+                             dtype_size=b.dtype_size)
+    assert need > 0
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v, f64=True)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = PA.paged_attention(qt, kt, vt, bt, sl)
+    check_close(out, ref, what=f"{dtype} D={head_size} library workspace")
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda)
+    out2 = PA.paged_attention(qt, kt, vt, bt, sl, workspace=ws)
+    check_close(out2, ref, what=f"{dtype} D={head_size} caller workspace")
+    with pytest.raises(PA.PagedAttentionError) as ei:
+        PA.paged_attention(qt, kt, vt, bt, sl,
+                           workspace=torch.empty(need + 16, dtype=torch.uint8, device=cuda)[4:])
+    assert ei.value.code == _native.NXT_PA_EINVAL
+    assert PA.device_status() == 0
+
+
 def test_prefix_shared_tables(cuda):
     b = W.config4(num_seqs=16)
     assert b.kv_bytes_unique() < b.kv_bytes()

@@ -6,13 +6,13 @@ a host that routes every device allocation through its own pool, cannot let a
 library call cudaMalloc (and cudaMalloc/cudaFree would synchronise the device
 in the middle of the decode loop). This entry point keeps its split-context
 partials in a fixed array compiled into the library. It is checked here
-through the C ABI against the regular entry point, on two calls in a row.
-This file is collected last on purpose.
+through the C ABI against the regular entry point and against the CPU oracle,
+on two calls in a row. This file is collected last on purpose.
 """
 import numpy as np
 import pytest
 
-from _helpers import check_close, to_device
+from _helpers import check_close, oracle_out, to_device
 from xllms_b200 import _native
 from xllms_b200 import operator_api as PA
 from xllms_b200 import workloads as W
@@ -37,6 +37,9 @@ CASES = {
                                       value_std=0.5),
     # fp32 MHA, CUDA-core kernel, split as well
     "generic_fp32": lambda: W.make_batch("na32", [2000, 33], 12, 12, 64, "f32", 92),
+    # odd head size, odd query heads, odd partition count: the (max, sum)
+    # pairs still start on an aligned boundary of the scratch
+    "generic_odd_d": lambda: W.make_batch("na33", [5000, 3, 2049], 3, 1, 33, "f16", 94),
 }
 
 
@@ -52,12 +55,45 @@ def test_noalloc_matches_regular_entry_point_on_two_calls(cuda, case):
     regular = PA.paged_attention(qt, kt, vt, bt, sl, num_blocks=b.num_blocks)
     torch.cuda.synchronize()
     expect = regular.float().cpu().numpy()
+    ref = oracle_out(b, q, k, v, f64=True)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     for call in range(2):
         out = torch.full_like(qt, float("nan"))
         assert _noalloc(b, qt, kt, vt, bt, sl, out, status) == _native.NXT_PA_OK
         torch.cuda.synchronize()
-        check_close(out, expect, what=f"{case} call {call + 1}")
+        check_close(out, expect, what=f"{case} call {call + 1} vs regular entry point")
+        check_close(out, ref, what=f"{case} call {call + 1} vs oracle")
+    assert int(status.item()) == 0
+
+
+def test_noalloc_follows_the_wait_budget(cuda):
+    """The thread's wait budget bounds this entry point's pipeline waits too:
+    a zero budget makes them run out (NXT_PA_DEV_TIMEOUT in the caller's
+    status word, no fault), and the next call with the budget restored is
+    correct again."""
+    import torch
+    lib = _native.xpa()
+    b = CASES["fast_fp16"]()
+    q, k, v = b.values_numpy()
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    assert PA.kernel_path(kt, vt, b.num_heads, b.head_size, b.num_kv_heads, b.block_size,
+                          b.dtype_size, b.kv_block_stride,
+                          b.kv_head_stride) == _native.NXT_PA_PATH_TMA_MMA
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = torch.empty_like(qt)
+    prev = lib.nxt_paged_attention_set_wait_budget_ns(0)
+    try:
+        assert _noalloc(b, qt, kt, vt, bt, sl, out, status) == _native.NXT_PA_OK
+        torch.cuda.synchronize()
+    finally:
+        lib.nxt_paged_attention_set_wait_budget_ns(prev)
+    assert int(status.item()) & _native.NXT_PA_DEV_TIMEOUT
+    status.zero_()
+    ref = oracle_out(b, q, k, v, f64=True)
+    for _ in range(2):
+        assert _noalloc(b, qt, kt, vt, bt, sl, out, status) == _native.NXT_PA_OK
+        torch.cuda.synchronize()
+        check_close(out, ref, what="after timeout")
     assert int(status.item()) == 0
 
 

@@ -57,6 +57,8 @@ namespace host {
 
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
+unsigned long long wait_budget_ns() { return g_wait_budget_ns; }
+
 }  // namespace host
 }  // namespace xpa
 
@@ -131,8 +133,7 @@ Plan make_plan(int B, int Hq, int D, int Hkv, int max_blocks, int nsm, int kv_es
   while (ceil_div(mb, pp) > 8192) pp <<= 1;
   pl.part_pages = pp;
   pl.max_parts = ceil_div(mb, pp);
-  if (pl.max_parts > 1)
-    pl.ws_bytes = (size_t)B * Hq * pl.max_parts * (size_t)(D + 2) * sizeof(float);
+  if (pl.max_parts > 1) pl.ws_bytes = partial_bytes((long long)B * Hq * pl.max_parts, D);
   return pl;
 }
 
@@ -276,6 +277,7 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   }
   int rc = check_args(out, q, k, v, bt, sl, B, Hq, D, Hkv, max_blocks, bs, ds, kbs, khs);
   if (rc != NXT_PA_OK || B == 0) return rc;
+  if (ws && !workspace_aligned(ws)) return NXT_PA_EINVAL;
   const int kv_fmt = kvq ? kvq->fmt : 0;
   const int kv_es = kvq ? 1 : ds;
   if (kvq) {
@@ -316,7 +318,7 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
                                             pre->max_group_size, pre->max_prefix_pages, sms));
     pchunks = ceil_div(pre->max_prefix_pages, pchunk);
     slots = pl.max_parts + pchunks;
-    pl.ws_bytes = (size_t)B * Hq * slots * (size_t)(D + 2) * sizeof(float);
+    pl.ws_bytes = partial_bytes((long long)B * Hq * slots, D);
   }
   if ((long long)B * Hkv * pl.max_parts > INT_MAX || (long long)B * Hq > INT_MAX)
     return NXT_PA_EINVAL;
@@ -358,7 +360,9 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   p.block_tables = bt;
   p.seq_lens = sl;
   p.part_o = static_cast<float*>(part);
-  p.part_ml = part ? static_cast<float*>(part) + (size_t)B * Hq * slots * D : nullptr;
+  p.part_ml = part ? reinterpret_cast<float*>(static_cast<char*>(part) +
+                                              part_ml_offset_bytes((long long)B * Hq * slots, D))
+                   : nullptr;
   p.status = status;
   p.kv_block_stride = kbs;
   p.kv_head_stride = khs;
@@ -630,8 +634,7 @@ size_t nxt_paged_attention_prefix_workspace_size(int num_seqs, int num_heads, in
                             sm_count_of(dev));
   const int pchunks =
       max_prefix_pages > 0 ? ceil_div(max_prefix_pages, prefix_chunk_pages(max_prefix_pages)) : 0;
-  return (size_t)num_seqs * num_heads * (pl.max_parts + pchunks) * (size_t)(head_size + 2) *
-         sizeof(float);
+  return partial_bytes((long long)num_seqs * num_heads * (pl.max_parts + pchunks), head_size);
 }
 
 int nxt_paged_attention_fp8_ex(void* out, const void* query, const void* key_cache,

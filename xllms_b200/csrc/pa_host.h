@@ -13,6 +13,28 @@ int ceil_div(long long a, long long b);
 // SM count of device `dev` (cached; 148 when the query fails).
 int sm_count_of(int dev);
 
+// Bound on every pipeline wait of kernels launched by this host thread
+// (nxt_paged_attention_set_wait_budget_ns; 1 s by default).
+unsigned long long wait_budget_ns();
+
+// Split-context partials of one call, in one workspace: part_o
+// [rows][slots][D] fp32 from byte 0, then part_ml [rows][slots][2] fp32 from
+// the next kPartAlign-byte boundary (rows = B * Hq). The merge reads (m, l)
+// as 8-byte pairs, which an odd rows * slots * D would otherwise misalign,
+// and part_o rows as 16-byte vectors, so the workspace itself must start on a
+// 16-byte boundary.
+constexpr size_t kPartAlign = 256;
+inline size_t part_ml_offset_bytes(long long row_slots, int D) {
+  const size_t o = (size_t)row_slots * (size_t)D * sizeof(float);
+  return (o + kPartAlign - 1) / kPartAlign * kPartAlign;
+}
+inline size_t partial_bytes(long long row_slots, int D) {
+  return part_ml_offset_bytes(row_slots, D) + (size_t)row_slots * 2 * sizeof(float);
+}
+inline bool workspace_aligned(const void* ws) {
+  return (reinterpret_cast<size_t>(ws) & 15u) == 0;
+}
+
 // Context partitioning of one call and the split-context partial bytes it needs.
 struct Plan {
   int part_pages = 32;

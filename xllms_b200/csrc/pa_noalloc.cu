@@ -27,14 +27,15 @@ namespace {
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NXT_PA_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-constexpr unsigned long long kWaitBudgetNs = 1000000000ull;  // 1 s per pipeline wait
 
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices];  // device address of the array, per device
 
 // Set-up, once per device, with that device current: look up the array's
 // device address. May load this module onto the device, so a caller should
-// make its first call on each device before any stream capture.
+// make its first call on each device before any stream capture. The address
+// is kept until the process exits; a cudaDeviceReset unloads the module and
+// leaves it stale, so the entry point is not for use across a reset.
 int scratch_address(int dev, void** out) {
   if (dev < 0 || dev >= kMaxDevices) return NXT_PA_EINVAL;
   std::lock_guard<std::mutex> lk(g_mu);
@@ -86,13 +87,15 @@ extern "C" int nxt_paged_attention_noalloc(
   p.block_tables = block_tables;
   p.seq_lens = seq_lens;
   p.part_o = static_cast<float*>(scratch);
-  p.part_ml = scratch ? static_cast<float*>(scratch) + (size_t)B * Hq * pl.max_parts * D
+  p.part_ml = scratch ? reinterpret_cast<float*>(
+                            static_cast<char*>(scratch) +
+                            part_ml_offset_bytes((long long)B * Hq * pl.max_parts, D))
                       : nullptr;
   p.status = device_status;
   p.kv_block_stride = kv_block_stride;
   p.kv_head_stride = kv_head_stride;
   p.num_blocks = num_blocks;
-  p.timeout_ns = kWaitBudgetNs;
+  p.timeout_ns = wait_budget_ns();
   p.B = B;
   p.Hq = Hq;
   p.Hkv = Hkv;
