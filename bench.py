@@ -10,15 +10,28 @@ context U[1024, 8192]). With N > 1 (launched by torch.distributed.run, one
 rank per GPU) the batch grows to 64*N sequences and the 8 KV heads are
 sharded over the ranks (KV-head-group sharding): per-GPU work stays that of
 config 2 ("scaling": "weak"), each rank holds its own page pool and block
-tables, and the outputs are all-gathered over NCCL into [B, Hq, D].
+tables, and every rank's kernels store its heads' output rows into every
+GPU's [B, Hq, D] buffer over NVLink (the fused head gather; --gather nccl
+runs an NCCL all-gather + head interleave instead). --workload c5 is config 5
+(B = 512 fixed, 64/8 heads, context U[4096, 16384]) split over the N GPUs
+("scaling": "strong").
+
+Every run checks its own output outside the timed regions: on each rank a
+sample of sequences of the gathered [B, Hq, D] output is compared with the
+CPU oracle over that rank's pools (its heads), and every rank's gathered
+buffer must equal every other's bit for bit. The line carries parity_ok and
+parity_worst; the process exits non-zero when the check fails.
 
 Printed by rank 0: one JSON line. `value` is algorithmic GB/s of the whole
 job (KV + Q + out + block tables + seq_lens) with inputs resident in HBM,
 device-timed with CUDA events, max over ranks. `e2e` is the same metric
 through the backend plugin's C ABI with Q / block tables / seq_lens copied
-host->device and the output device->host inside every step. `roofline`
-covers the attention kernel alone (events recorded around it by the
-library). `cpu_baseline` times the reference's CPU attention on the host.
+host->device and the output device->host inside every step (K steps
+enqueued back to back; `e2e.host_synced` waits on the host for each step's
+output before the next, as a decode loop does). `roofline` covers the
+attention kernel alone (events recorded around it by the library);
+`per_rank` splits a step into attention, merge and gather-barrier time on
+every rank. `cpu_baseline` times the reference's CPU attention on the host.
 """
 from __future__ import annotations
 
@@ -70,6 +83,12 @@ def parse_args():
     ap.add_argument("--prefix", choices=["on", "off"], default="on",
                     help="c4: on = shared-prefix (cascade) attention over the radix prefix "
                          "groups (nxt_paged_attention_prefix_ex); off = plain decode kernels")
+    ap.add_argument("--shard-of", type=int, default=0, metavar="P",
+                    help="1 GPU, c2/c5: run rank 0's shard of the P-GPU workload alone, with no "
+                         "gather (the per-GPU work of a P-GPU run without its exchange)")
+    ap.add_argument("--seed", type=int, default=None,
+                    help="c2/c5: another seed for the lengths, tables and values of the "
+                         "workload (default: the configuration's own)")
     ap.add_argument("--seqs", type=int, default=0,
                     help="sequences per GPU for c2/c4/c5 (default: the BASELINE size); smaller "
                          "values make the small cases the ncu captures run on")
@@ -85,10 +104,21 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def build_id():
+    """Identity of the loaded kernel build (sources + flags), written by the
+    library's Makefile next to the libraries; None when absent."""
+    try:
+        with open(os.path.join(ROOT, "xllms_b200", "_lib", "build_id")) as f:
+            return f.read().strip() or None
+    except OSError:
+        return None
+
+
 def ncu_traffic(workload_name: str, alg_bytes: int):
     """DRAM read + write bytes per launch of the attention kernel from the ncu
     capture recorded in profiles/traffic.json, when it was taken on this exact
-    workload (same algorithmic bytes); else None."""
+    workload (same algorithmic bytes) with this exact build (same build id);
+    else None."""
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
             rec = json.load(f).get(workload_name)
@@ -96,15 +126,19 @@ def ncu_traffic(workload_name: str, alg_bytes: int):
         return None
     if not rec or int(rec["algorithmic_bytes_per_launch"]) != int(alg_bytes):
         return None
+    bid = build_id()
+    if bid is None or rec.get("build_id") != bid:
+        return None
     return int(rec["dram_read_bytes_per_launch"]) + int(rec["dram_write_bytes_per_launch"])
 
 
-def make_batch(workload: str, world: int, rank: int, seqs: int = 0):
+def make_batch(workload: str, world: int, rank: int, seqs: int = 0, seed=None):
     from xllms_b200 import workloads as W
+    kw = {} if seed is None else {"seed": seed}
     if workload == "c2":
-        return W.config2(num_seqs=(seqs or 64) * world, world_size=world, rank=rank)
+        return W.config2(num_seqs=(seqs or 64) * world, world_size=world, rank=rank, **kw)
     if workload == "c5":
-        return W.config5(world_size=world, rank=rank, num_seqs=seqs or 512)
+        return W.config5(world_size=world, rank=rank, num_seqs=seqs or 512, **kw)
     if world > 1:
         raise SystemExit(f"workload {workload} runs on one GPU")
     if workload == "c4" and seqs:
@@ -343,6 +377,56 @@ def cpu_leg(batch, arrays, seconds: float = 0.0, passes: int = 0, warmup: int = 
     return sub_bytes / per / 1e9, per, info
 
 
+# ── output check (outside the timed regions) ──────────────────────────────
+PARITY_RTOL = 1e-3  # north_star: 1e-3 relative error, fp32 accumulation
+_PARITY_OK = True    # set by the output check; a failed check makes the exit status 1
+
+
+def parity_sample(num_seqs: int):
+    """Sequences the output check compares with the oracle: first, last and
+    two in between."""
+    return sorted({0, num_seqs // 3, (2 * num_seqs) // 3, num_seqs - 1})
+
+
+def verify_output(batch, q, k, v, full, rank, world, dev, kv_fmt=None, k_scale=1.0,
+                  v_scale=1.0):
+    """Checks the step's output `full` [B, Hq_total, D] (this rank's gathered
+    buffer; the plain output at N = 1). Rank r compares its own heads of the
+    parity_sample sequences with the fp64 CPU oracle over its own pools, and
+    (N > 1) every rank's buffer must equal this one bit for bit, so together
+    every head of every buffer is covered. Returns (ok, worst) reduced over
+    the ranks; worst = max |x - ref| / (rtol * max(|ref|, eps))."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from _helpers import gather_subset
+    seqs = parity_sample(batch.num_seqs)
+    qs, ks, vs, bt, sl = gather_subset(batch, seqs, q, k, v)
+    if kv_fmt:
+        fmt = {"e4m3": O.FP8_E4M3, "e5m2": O.FP8_E5M2, "int8": O.KV_INT8}[kv_fmt]
+        ref = O.attention_fp8(qs, ks, vs, fmt, k_scale, v_scale, bt, sl, batch.num_kv_heads,
+                              batch.scale, block_size=batch.block_size, f64=True)
+    else:
+        ref = O.attention(qs, ks, vs, bt, sl, batch.num_kv_heads, batch.scale,
+                          block_size=batch.block_size, f64=True, threads=host_cores())
+    h0 = rank * batch.num_heads
+    got = full[seqs][:, h0:h0 + batch.num_heads].float().cpu().numpy()
+    ok, worst = O.rel_err_ok(got, ref, PARITY_RTOL)
+    ok = bool(ok) and bool(np.isfinite(got).all())
+    if world > 1:
+        import torch.distributed as dist
+        # bit patterns, widened to int32 (every backend gathers int32)
+        mine = full.contiguous().view(torch.int16).reshape(-1).to(torch.int32)
+        every = torch.empty(world * mine.numel(), dtype=mine.dtype, device=dev)
+        dist.all_gather_into_tensor(every, mine)
+        ok = ok and bool((every.view(world, -1) == mine.unsqueeze(0)).all())
+        t = torch.tensor([0.0 if ok else 1.0, float(worst)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ok, worst = t[0].item() == 0.0, t[1].item()
+    return ok, float(worst)
+
+
 # ── our implementation ─────────────────────────────────────────────────────
 def run_ours(args, rank, world, local_rank):
     import torch
@@ -353,7 +437,12 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    batch = make_batch(args.workload, world, rank, args.seqs)
+    if args.shard_of > 1:
+        if world > 1 or args.workload not in ("c2", "c5"):
+            raise SystemExit("--shard-of runs one shard of c2 / c5 on one GPU")
+        batch = make_batch(args.workload, args.shard_of, 0, args.seqs, args.seed)
+    else:
+        batch = make_batch(args.workload, world, rank, args.seqs, args.seed)
     fp8 = args.kv != "fp16"
     if fp8 and (world > 1 or args.workload in ("c1", "c4")):
         raise SystemExit("--kv e4m3 / e5m2 / int8 runs configs 2, 3 and 5 on one GPU")
@@ -444,6 +533,7 @@ def run_ours(args, rank, world, local_rank):
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     c0 = ClockSampler.now()
+    torch.cuda.nvtx.range_push("timed steps")
     start.record()
     for _ in range(K):
         if graph is not None:
@@ -451,26 +541,39 @@ def run_ours(args, rank, world, local_rank):
         else:
             step()
     stop.record()
+    torch.cuda.nvtx.range_pop()
     barrier()
     c1 = ClockSampler.now()
     t_step = start.elapsed_time(stop) / K
-    # output of the device-resident run
+    # output of the device-resident run, checked against the oracle
     resident = (fg.output(fg.step) if fused else (full if world > 1 else out)).clone()
+    parity = verify_output(batch, q, k, v, resident, rank, world, dev,
+                           kv_fmt=args.kv if fp8 else None,
+                           k_scale=k_scale if fp8 else 1.0, v_scale=v_scale if fp8 else 1.0)
 
     # Timed region 2: K steps with events recorded by the library right around
     # the attention kernel -> its own mean duration for the roofline. (Kept
     # out of region 1: an event between the attention kernel and the merge
     # kernel stops the merge's programmatic launch from overlapping the tail.)
-    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    for e in ev_a + ev_b:
+    # The library records ev_a / ev_b around the attention kernel and ev_c
+    # after the merge; ev_d closes the step (after the fused gather's barrier,
+    # or the NCCL gather), which gives the per-rank split of a step.
+    ev_a, ev_b, ev_c, ev_d = ([torch.cuda.Event(enable_timing=True) for _ in range(K)]
+                              for _ in range(4))
+    for e in ev_a + ev_b + ev_c + ev_d:
         e.record()  # materialise the CUDA event handles
     barrier()
+    torch.cuda.nvtx.range_push("profiled steps")
     for i in range(K):
-        lib.nxt_paged_attention_profile_next(ev_a[i].cuda_event, ev_b[i].cuda_event)
+        lib.nxt_paged_attention_profile_next_ex(ev_a[i].cuda_event, ev_b[i].cuda_event,
+                                                ev_c[i].cuda_event)
         step()
+        ev_d[i].record()
+    torch.cuda.nvtx.range_pop()
     barrier()
     t_kern = statistics.mean(a.elapsed_time(b) for a, b in zip(ev_a, ev_b))
+    split = [statistics.mean(a.elapsed_time(b) for a, b in zip(x, y))
+             for x, y in ((ev_a, ev_b), (ev_b, ev_c), (ev_c, ev_d))]
     st = PA.device_status(clear=True)
     if st:
         raise SystemExit(f"device status after timing: {st:#x}")
@@ -481,7 +584,8 @@ def run_ours(args, rank, world, local_rank):
             fg.close(dist.barrier)
         sampler.close()
         return _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, None,
-                       sampler.summary(c0, c1), None, q, k, v, 0, 0, dev, cascade)
+                       sampler.summary(c0, c1), None, q, k, v, 0, 0, dev, cascade,
+                       parity=parity, split=split)
     plugin = PA.CudaBackendPlugin()
     # One pinned staging buffer holds the step's inputs (Q | block tables |
     # seq_lens), so each step issues a single host->device copy; the device
@@ -539,15 +643,29 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0 = ClockSampler.now()
+    torch.cuda.nvtx.range_push("e2e steps")
     e_start.record()
     for _ in range(K):
         e2e_step()
     e_stop.record()
+    torch.cuda.nvtx.range_pop()
     barrier()
     e1 = ClockSampler.now()
+    # The same steps with the host waiting for each step's output before it
+    # enqueues the next, as a decode loop must (the idle gaps are timed too).
+    h_start, h_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("e2e host-synced steps")
+    h_start.record()
+    for _ in range(K):
+        e2e_step()
+        torch.cuda.current_stream().synchronize()
+    h_stop.record()
+    torch.cuda.nvtx.range_pop()
+    barrier()
     sampler.close()
     clocks, clocks_e2e = sampler.summary(c0, c1), sampler.summary(e0, e1)
     t_e2e = e_start.elapsed_time(e_stop) / K
+    t_e2e_sync = h_start.elapsed_time(h_stop) / K
     if not torch.equal(out_h.to(dev), resident):
         raise SystemExit("e2e output differs from the device-resident run")
     plugin.close()
@@ -556,22 +674,34 @@ def run_ours(args, rank, world, local_rank):
     h2d = stage_h.numel()
     d2h = out_h.numel() * out_h.element_size()
     return _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t_e2e,
-                   clocks, clocks_e2e, q, k, v, h2d, d2h, dev, cascade)
+                   clocks, clocks_e2e, q, k, v, h2d, d2h, dev, cascade, parity=parity,
+                   split=split, t_e2e_sync=t_e2e_sync)
 
 
 def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t_e2e, clocks,
-            clocks_e2e, q, k, v, h2d, d2h, dev, cascade=False):
+            clocks_e2e, q, k, v, h2d, d2h, dev, cascade=False, parity=(True, 0.0), split=None,
+            t_e2e_sync=None):
     import torch
     import torch.distributed as dist
     K = args.steps
     bytes_rank = batch.algorithmic_bytes()
     ub_rank = batch.algorithmic_bytes(unique=True) if args.workload == "c4" else bytes_rank
     kv_rank = batch.kv_bytes()
+    global _PARITY_OK
+    _PARITY_OK = bool(parity[0])
+    split = split or [0.0, 0.0, 0.0]
+    per_rank = [split]
     if world > 1:
-        t = torch.tensor([t_step, t_kern, t_e2e or 0.0], dtype=torch.float64, device=dev)
+        t = torch.tensor([t_step, t_kern, t_e2e or 0.0, t_e2e_sync or 0.0], dtype=torch.float64,
+                         device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_step, t_kern, t_e2e = (float(x) for x in t.tolist())
+        t_step, t_kern, t_e2e, t_e2e_sync = (float(x) for x in t.tolist())
         t_e2e = t_e2e or None
+        t_e2e_sync = t_e2e_sync or None
+        mine = torch.tensor(split, dtype=torch.float64, device=dev)
+        every = torch.empty(world * 3, dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(every, mine)
+        per_rank = every.view(world, 3).tolist()
         s = torch.tensor([bytes_rank, ub_rank, kv_rank, h2d, d2h], dtype=torch.float64,
                          device=dev)
         dist.all_reduce(s, op=dist.ReduceOp.SUM)
@@ -599,7 +729,7 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
         "warmup": args.warmup,
         "ms_per_step": round(t_step, 5),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.workload == "c5" else "weak",
         "vs_baseline": None,
         "dtype": "f16" if batch.kv_elem_size != 1 else
                  f"f16 (Q, out), {_kv_label(batch.notes['kv_format'])} KV",
@@ -631,6 +761,8 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
                     (f" ({_kv_label(batch.notes['kv_format'])} KV variant)"
                      if batch.kv_elem_size == 1 else ""),
             "kv_cache": batch.notes.get("kv_format", "fp16"),
+            **({"shard_of": args.shard_of} if args.shard_of > 1 else {}),
+            **({"seed": args.seed} if args.seed is not None else {}),
         },
         "pct_hbm_peak": round(100.0 * (tot_ub / world) / (t_step * 1e-3) / 1e9 / peak, 2),
         "seq_tokens_per_s": round(seqs_total / (t_step * 1e-3), 1),
@@ -648,6 +780,7 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
                            else "fallback 6.65 TB/s",
             "kernel_ms": round(t_kern, 5),
             "traffic": ncu_traffic(batch.name, ub_rank),
+            "build_id": build_id(),
             "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
             "bytes_per_launch": ub_rank,
         },
@@ -666,6 +799,27 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
                     "nxt_backend_run (libxllm_cuda_backend.so); per step one pinned H2D copy "
                     "(Q, block tables, seq_lens) and one D2H copy of the output"),
             "clocks": clocks_e2e,
+            "host_synced": None if t_e2e_sync is None else {
+                "value": round(tot_bytes / (t_e2e_sync * 1e-3) / 1e9, 2),
+                "ms_per_step": round(t_e2e_sync, 5),
+                "what": "the same steps, the host waiting for each step's output before "
+                        "enqueueing the next (idle gaps included)",
+            },
+        },
+        "parity_ok": bool(parity[0]),
+        "parity_worst": round(float(parity[1]), 4),
+        "parity_check": (f"sequences {parity_sample(batch.num_seqs)} of the gathered output vs "
+                         f"the fp64 CPU oracle over each rank's pools, |x-ref| <= "
+                         f"{PARITY_RTOL:g}*max(|ref|, 0.01*rms(ref)); worst = largest "
+                         "|x-ref| / that bound (<= 1 passes)" +
+                         ("; every rank's gathered buffer bitwise equal" if world > 1 else "")),
+        "per_rank": {
+            "attn_ms": [round(x[0], 5) for x in per_rank],
+            "merge_ms": [round(x[1], 5) for x in per_rank],
+            "barrier_ms": [round(x[2], 5) for x in per_rank],
+            "what": "mean per step over K steps with events between the kernels: attention "
+                    "kernel; split-context merge; from the merge to the end of the step (the "
+                    "fused gather's cross-GPU barrier, or the NCCL all-gather + interleave)",
         },
         "clocks": clocks,
         "gpu_launches": launches_per_step * K * world,
@@ -684,7 +838,7 @@ def run_reference(args, rank, world):
     sample pass per step."""
     if rank != 0:
         return None
-    batch = make_batch(args.workload, world, 0, args.seqs)
+    batch = make_batch(args.workload, world, 0, args.seqs, args.seed)
     arrays = sample_arrays(batch, 8)
     seqs = len(arrays[4])
     gbs, per, info = cpu_leg(batch, arrays, passes=max(1, args.steps), warmup=args.warmup)
@@ -841,6 +995,9 @@ def main():
             dist.destroy_process_group()
     if line is not None:
         print(json.dumps(line), flush=True)
+    if not _PARITY_OK:
+        print(f"rank {rank}: output check against the oracle failed", file=sys.stderr)
+        sys.exit(1)
 
 
 if __name__ == "__main__":

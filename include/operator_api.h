@@ -521,6 +521,16 @@ int nxt_paged_attention_fp8_sharded(
  * request is consumed by that one call. NULL, NULL cancels a pending request. */
 int nxt_paged_attention_profile_next(void *before, void *after);
 
+/* extension — as nxt_paged_attention_profile_next, plus `after_merge`,
+ * recorded after the split-context reduce (after the attention kernel when the
+ * call launches no reduce) and ahead of the fused head gather's end-of-step
+ * barrier of a sharded call. An event recorded after the call returns then
+ * closes the barrier's share. Any of the three may be NULL. The events sit
+ * between kernels that otherwise overlap by programmatic dependent launch, so
+ * the three shares add up to a little more than an unprofiled call. */
+int nxt_paged_attention_profile_next_ex(void *before, void *after_attention,
+                                        void *after_merge);
+
 /* extension — the calling thread's current CUDA device: its ordinal, SM count
  * and name (name_len bytes at most, NUL-terminated). Used by the backend
  * plugin's init. Returns NXT_PA_OK, or NXT_PA_ECUDA when no device is usable. */

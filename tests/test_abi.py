@@ -92,7 +92,7 @@ def test_invalid_arguments_rejected_before_any_launch(bad):
     assert ei.value.code == _native.NXT_PA_EINVAL
 
 
-def _plan_parts(B, Hkv, max_blocks, per_sm=12, nsm=148, part_pages=128):
+def _plan_parts(B, Hkv, max_blocks, per_sm=24, nsm=148, part_pages=128):
     """Partition count of one call: the library's planning rule restated
     (partitions halve, down to 4 pages, while the grid holds fewer than
     per_sm items per SM; the SM count is 148 when no device answers)."""

@@ -202,3 +202,51 @@ def test_fused_head_gather_class_one_rank(cuda):
                    b.scale, b.num_blocks)
     finally:
         fg.close()
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_config5_shape_emulated_ranks(cuda, world):
+    """BASELINE config 5 at full size (B = 512, 64 query / 8 KV heads, D 128,
+    fp16, context U[4096, 16384]) with `world` ranks emulated on one GPU, as
+    at 2 and 8 GPUs: each rank's own pool and block tables (its KV heads),
+    its launch storing into every rank's [512, 64, 128] gather buffer. A
+    sample of sequences of each rank's heads is checked against the fp64
+    oracle over that rank's pools, and every buffer must equal every other
+    bit for bit, so every head of every buffer is covered. Ranks run one
+    after another (their signals set on the host), holding one rank's
+    pools at a time."""
+    import torch
+    from _helpers import gather_subset
+    lib = _native.xpa()
+    H, D = 64, 128
+    bufs, half, flags_off = _buffers(lib, 512, H, D, 2, world)
+    shards = _shards(bufs, flags_off, H, world)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    seqs = [0, 170, 341, 511]
+    try:
+        for r in range(world):
+            _flags(bufs[r] + flags_off, world, cuda).fill_(1)
+        for r in range(world):
+            b = W.config5(world_size=world, rank=r)
+            assert b.num_seqs == 512 and b.num_heads == H // world
+            q, k, v = b.values_torch(cuda)
+            bt, sl = b.tables_torch(cuda)
+            assert _call(lib, shards[r], 1, b, q, k, v, bt, sl, status) == 0
+            torch.cuda.synchronize()
+            qs, ks, vs, bts, sls = gather_subset(b, seqs, q, k, v)
+            ref = O.attention(qs, ks, vs, bts, sls, b.num_kv_heads, b.scale, f64=True)
+            view = torch.as_tensor(S._DeviceArray(bufs[0] + half, (512, H, D), "<f2"),
+                                   device=cuda)
+            h0 = r * b.num_heads
+            check_close(view[seqs][:, h0:h0 + b.num_heads], ref, what=f"rank {r} of {world}")
+            del q, k, v
+        first = torch.as_tensor(S._DeviceArray(bufs[0] + half, (512, H, D), "<i2"), device=cuda)
+        for r in range(1, world):
+            other = torch.as_tensor(S._DeviceArray(bufs[r] + half, (512, H, D), "<i2"),
+                                    device=cuda)
+            assert torch.equal(first, other), f"buffer {r} differs from buffer 0"
+        assert int(status.item()) == 0
+    finally:
+        torch.cuda.synchronize()
+        for p in bufs:
+            lib.nxt_pa_peer_free(p)

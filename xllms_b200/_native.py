@@ -73,6 +73,7 @@ SIGNATURES = {
          _VP, _VP],
     ),
     "nxt_paged_attention_profile_next": (_I, [_VP, _VP]),
+    "nxt_paged_attention_profile_next_ex": (_I, [_VP, _VP, _VP]),
     "nxt_block_tables_layout": (_SZ, [_I, _I, _I, _VP]),
     "nxt_block_tables_staging_size": (_SZ, [_I, _I]),
     "nxt_build_block_tables": (

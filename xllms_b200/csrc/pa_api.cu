@@ -27,6 +27,7 @@ namespace {
 thread_local int g_last_error = NXT_PA_OK;
 thread_local cudaEvent_t g_prof_before = nullptr;  // one-shot timing events
 thread_local cudaEvent_t g_prof_after = nullptr;
+thread_local cudaEvent_t g_prof_merged = nullptr;
 
 constexpr unsigned long long kWaitBudgetNs = 1000000000ull;  // 1 s per pipeline wait
 thread_local unsigned long long g_wait_budget_ns = kWaitBudgetNs;
@@ -107,20 +108,39 @@ int sm_count_of(int dev) {
   return d.sm_count;
 }
 
+// Sharded calls on several GPUs: 1 = every output row is stored (to every
+// peer) by the merge kernel, 0 = single-partition rows by the attention kernel.
+#ifndef XPA_SHARD_MERGE_ALL
+#define XPA_SHARD_MERGE_ALL 1
+#endif
+
+// 1: the first attention kernel of a plain call is launched as a
+// programmatic dependent of the stream's previous kernel and waits for it
+// before reading anything (hides its launch latency); 0: an ordinary launch.
+#ifndef XPA_EARLY_LAUNCH
+#define XPA_EARLY_LAUNCH 1
+#endif
+
 // Partition size: XPA_PART_PAGES by default, halved (down to 4 pages) while
-// the grid would hold fewer than 12 items per SM (about two waves of the
-// TMA kernel's 6 resident CTAs per SM), and doubled while the reduce kernel's
-// per-row weight table would not fit its shared memory.
+// the grid would hold fewer than XPA_MIN_ITEMS_PER_SM items per SM, and
+// doubled while a row would have more than 8192 partitions.
 // Default partition length in pages (128 pages = 2048 tokens at page size 16);
 // a build may override it with -DXPA_PART_PAGES=n for tuning sweeps.
 #ifndef XPA_PART_PAGES
 #define XPA_PART_PAGES 128
 #endif
 
+// Items per SM before partitions stop shrinking: 24 (four per resident
+// fp16 CTA). A CTA streams a 128-page item in ~140 us when every slot is
+// busy, so with few, long items per slot the grid's last items run on a
+// half-idle GPU. Measured on B200 over five seeded config-2 batches:
+// 128-page partitions (the old floor of 12 items per SM) gave 0.91-1.01 of
+// the copy peak, 64-page ones 0.99-1.00, on 1 GPU and on an 8-GPU shard.
+#ifndef XPA_MIN_ITEMS_PER_SM
+#define XPA_MIN_ITEMS_PER_SM 24
+#endif
 // fp8 pages stream in half the time, so the grid needs more CTAs per SM
-// before partitions stop shrinking (measured at config 2: 128-page
-// partitions 0.1675 ms, 64-page 0.1591 ms; at configs 3 and 5, which already
-// have > 24 CTAs per SM, shorter partitions only add merge work).
+// before partitions stop shrinking.
 #ifndef XPA_FP8_MIN_ITEMS_PER_SM
 #define XPA_FP8_MIN_ITEMS_PER_SM 24
 #endif
@@ -128,7 +148,8 @@ Plan make_plan(int B, int Hq, int D, int Hkv, int max_blocks, int nsm, int kv_es
   Plan pl;
   const long long mb = max_blocks > 0 ? max_blocks : 1;
   int pp = XPA_PART_PAGES;
-  const long long min_items = (long long)(kv_es == 1 ? XPA_FP8_MIN_ITEMS_PER_SM : 12) * nsm;
+  const long long min_items =
+      (long long)(kv_es == 1 ? XPA_FP8_MIN_ITEMS_PER_SM : XPA_MIN_ITEMS_PER_SM) * nsm;
   while (pp > 4 && (long long)B * Hkv * ceil_div(mb, pp) < min_items) pp >>= 1;
   while (ceil_div(mb, pp) > 8192) pp <<= 1;
   pl.part_pages = pp;
@@ -320,6 +341,10 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
     slots = pl.max_parts + pchunks;
     pl.ws_bytes = partial_bytes((long long)B * Hq * slots, D);
   }
+  // Sharded calls over several GPUs store every row through the merge, so
+  // the attention kernel's CTAs never wait on stores to peers' memory.
+  const bool merge_all = shard && shard->world_size > 1 && XPA_SHARD_MERGE_ALL;
+  if (merge_all && pl.ws_bytes == 0) pl.ws_bytes = partial_bytes((long long)B * Hq * slots, D);
   if ((long long)B * Hkv * pl.max_parts > INT_MAX || (long long)B * Hq > INT_MAX)
     return NXT_PA_EINVAL;
 
@@ -384,6 +409,10 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
   p.kv_fmt = kv_fmt;
   p.v_scale = kvq ? kvq->v_scale : 1.f;
   p.after_append = after_append ? 1 : 0;
+  p.merge_all = merge_all ? 1 : 0;
+  // The first kernel of a plain call (not after an append, not a cascade)
+  // becomes resident while the stream's previous kernel finishes.
+  p.wait_first = (!pre && !after_append && XPA_EARLY_LAUNCH) ? 1 : 0;
   {
     auto a16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
     bool ok = D % 8 == 0 && a16(part);
@@ -402,8 +431,8 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
     for (int r = 0; r < shard->world_size; ++r) p.peers[r] = shard->peer_out[r];
   }
 
-  cudaEvent_t ev_a = g_prof_before, ev_b = g_prof_after;
-  g_prof_before = g_prof_after = nullptr;
+  cudaEvent_t ev_a = g_prof_before, ev_b = g_prof_after, ev_c = g_prof_merged;
+  g_prof_before = g_prof_after = g_prof_merged = nullptr;
   if (ev_a && cudaEventRecord(ev_a, st) != cudaSuccess) return NXT_PA_ECUDA;
   cudaError_t e;
   if (pre) {
@@ -438,10 +467,11 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
     if (e != cudaSuccess) return map_cuda(e);
   }
   if (ev_b && cudaEventRecord(ev_b, st) != cudaSuccess) return NXT_PA_ECUDA;
-  if (pl.max_parts > 1 || pre) {
+  if (pl.max_parts > 1 || pre || merge_all) {
     e = xpa::launch_reduce(p, ds, st);
     if (e != cudaSuccess) return map_cuda(e);
   }
+  if (ev_c && cudaEventRecord(ev_c, st) != cudaSuccess) return NXT_PA_ECUDA;
   if (shard) {
     e = xpa::launch_peer_barrier(reinterpret_cast<void* const*>(shard->peer_flags),
                                  shard->world_size, shard->rank, step, status, g_wait_budget_ns,
@@ -851,6 +881,14 @@ uint64_t nxt_paged_attention_set_wait_budget_ns(uint64_t budget_ns) {
 int nxt_paged_attention_profile_next(void* before, void* after) {
   g_prof_before = static_cast<cudaEvent_t>(before);
   g_prof_after = static_cast<cudaEvent_t>(after);
+  g_prof_merged = nullptr;
+  return NXT_PA_OK;
+}
+
+int nxt_paged_attention_profile_next_ex(void* before, void* after_attention, void* after_merge) {
+  g_prof_before = static_cast<cudaEvent_t>(before);
+  g_prof_after = static_cast<cudaEvent_t>(after_attention);
+  g_prof_merged = static_cast<cudaEvent_t>(after_merge);
   return NXT_PA_OK;
 }
 

@@ -55,6 +55,15 @@ struct Params {
   // griddepcontrol.wait (the appended token lives there).
   int after_append;
   int join_primary;  // CTA 0 waits for the preceding grid before it exits
+  // 1: no row is written by the attention kernel; rows of single-partition
+  // sequences leave a one-slot partial and the merge writes every row (the
+  // fused head gather keeps peer stores out of the attention kernel this way)
+  int merge_all;
+  // 1: this grid was launched as a programmatic dependent of whatever kernel
+  // precedes the call on the stream, so that its CTAs are resident before
+  // that kernel ends; every CTA waits for it (griddepcontrol.wait) before it
+  // reads anything. Only the launch latency is hidden, no work overlaps.
+  int wait_first;
   // Quantised KV cache: 0 = K/V in the query's dtype; kKvE4M3 / kKvE5M2 /
   // kKvInt8 = one byte per element holding encode(x / scale). k_scale is folded into
   // scale_log2; v_scale multiplies V (generic path) or O (fast path).
@@ -126,7 +135,7 @@ __device__ __forceinline__ ItemKind decode_item(const Params& p, int idx, Item& 
   const int P = prefix_of(p, it.b, npages);
   it.nparts = (npages - P + p.part_pages - 1) / p.part_pages;
   it.slot0 = P > 0 ? (P + p.prefix_chunk - 1) / p.prefix_chunk : 0;
-  it.direct = (P == 0 && it.nparts == 1) ? 1 : 0;
+  it.direct = (P == 0 && it.nparts == 1 && !p.merge_all) ? 1 : 0;
   if (it.nparts == 0) return (it.part == 0 && npages == 0) ? kItemZero : kItemNone;
   if (it.part >= it.nparts) return kItemNone;
   it.page_begin = P + it.part * p.part_pages;

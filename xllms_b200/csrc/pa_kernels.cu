@@ -48,6 +48,7 @@ __global__ void __launch_bounds__(128) pa_generic_kernel(const Params p) {
   __shared__ float sm_l[NW][HG];
 
   pdl_launch_dependents();
+  if (p.wait_first) pdl_wait_primary();
   Item it;
   const ItemKind kind = decode_item(p, blockIdx.x, it);
   if (kind == kItemNone) return;
@@ -243,6 +244,7 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
   int* meta = reinterpret_cast<int*>(smem + C::kBarOff + STAGES * 16);
 
   pdl_launch_dependents();
+  if (p.wait_first) pdl_wait_primary();
   Item it;
   const ItemKind kind = decode_item(p, blockIdx.x, it);
   if (kind == kItemNone) return;
@@ -722,7 +724,8 @@ __global__ void __launch_bounds__(128) pa_reduce_kernel(const Params p) {
     const int P = prefix_of(p, b, npages);
     const int nparts = (npages - P + p.part_pages - 1) / p.part_pages;
     nslots = (P > 0 ? (P + p.prefix_chunk - 1) / p.prefix_chunk : 0) + nparts;
-    direct = P == 0 && nparts <= 1;  // written directly by the attention kernel
+    // written directly by the attention kernel (zero rows always are)
+    direct = P == 0 && (nparts == 0 || (nparts == 1 && !p.merge_all));
   }
   pdl_launch_dependents();  // the gather barrier (if any) may be scheduled now
   // Every CTA waits for the attention grid, also those with nothing to merge:
@@ -731,6 +734,121 @@ __global__ void __launch_bounds__(128) pa_reduce_kernel(const Params p) {
   pdl_wait_primary();
   if (direct) return;
   merge_row_warp<T>(p, row, nslots, lane, sw[warp]);
+}
+
+// ════════════════════════════════════════════════════════════════════════
+// The same merge for rows with many partials (long contexts split into tens
+// of partitions): one CTA of four warps per (b, q head) row. Warp w
+// accumulates slots w, w + 4, ... (each lane 4 consecutive elements, four
+// slots' loads in flight), so a row's partials are read by four warps at
+// once instead of one; the four partial sums meet in shared memory.
+// ════════════════════════════════════════════════════════════════════════
+template <typename T>
+__global__ void __launch_bounds__(128) pa_reduce_wide_kernel(const Params p) {
+  constexpr int NW = 4;
+  __shared__ float s_num[NW][256];
+  __shared__ float s_den[NW];
+  __shared__ float s_max[NW];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = blockIdx.x;
+  const int b = (int)(row / p.Hq);
+  int L = __ldg(p.seq_lens + b);
+  const long long lim = (long long)p.max_blocks * p.block_size;
+  L = L < 0 ? 0 : ((long long)L > lim ? (int)lim : L);
+  const int npages = (L + p.block_size - 1) / p.block_size;
+  const int P = prefix_of(p, b, npages);
+  const int nparts = (npages - P + p.part_pages - 1) / p.part_pages;
+  const int nslots = (P > 0 ? (P + p.prefix_chunk - 1) / p.prefix_chunk : 0) + nparts;
+  const bool direct = P == 0 && (nparts == 0 || (nparts == 1 && !p.merge_all));
+  pdl_launch_dependents();  // the gather barrier (if any) may be scheduled now
+  pdl_wait_primary();       // every CTA: this grid must not complete before the attention grid
+  if (direct) return;
+
+  const float2* ml = reinterpret_cast<const float2*>(p.part_ml) + row * p.slots;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < nslots; i += NW * 32) mx = fmaxf(mx, __ldcg(&ml[i].x));
+  mx = warp_max(mx);
+  if (lane == 0) s_max[warp] = mx;
+  __syncthreads();
+  const float M = fmaxf(fmaxf(s_max[0], s_max[1]), fmaxf(s_max[2], s_max[3]));
+  auto weight = [M](float m) { return (M == -INFINITY || m == -INFINITY) ? 0.f : ex2(m - M); };
+
+  const float* po = p.part_o + row * p.slots * p.D;
+  float den = 0.f;
+  const bool vec = (p.D & 3) == 0;  // part_o rows are 16-byte aligned when D % 4 == 0
+  for (int base = 0; base < p.D; base += vec ? 128 : 32) {
+    const int d0 = base + (vec ? lane * 4 : lane);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float dsum = 0.f;
+    int i = warp;
+    for (; i + 3 * NW < nslots; i += 4 * NW) {
+      float2 m4[4];
+      float4 x4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        m4[u] = __ldcg(ml + i + u * NW);
+        if (d0 < p.D) {
+          const float* src = po + (long long)(i + u * NW) * p.D + d0;
+          x4[u] = vec ? __ldcg(reinterpret_cast<const float4*>(src))
+                      : make_float4(__ldcg(src), 0.f, 0.f, 0.f);
+        } else {
+          x4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float w = weight(m4[u].x);
+        dsum = fmaf(w, m4[u].y, dsum);
+        acc.x = fmaf(w, x4[u].x, acc.x);
+        acc.y = fmaf(w, x4[u].y, acc.y);
+        acc.z = fmaf(w, x4[u].z, acc.z);
+        acc.w = fmaf(w, x4[u].w, acc.w);
+      }
+    }
+    for (; i < nslots; i += NW) {
+      const float2 m = __ldcg(ml + i);
+      const float w = weight(m.x);
+      dsum = fmaf(w, m.y, dsum);
+      if (d0 < p.D) {
+        const float* src = po + (long long)i * p.D + d0;
+        const float4 x = vec ? __ldcg(reinterpret_cast<const float4*>(src))
+                             : make_float4(__ldcg(src), 0.f, 0.f, 0.f);
+        acc.x = fmaf(w, x.x, acc.x);
+        acc.y = fmaf(w, x.y, acc.y);
+        acc.z = fmaf(w, x.z, acc.z);
+        acc.w = fmaf(w, x.w, acc.w);
+      }
+    }
+    if (base == 0) den = dsum;  // every pass sums the same weights
+    if (d0 < p.D) {
+      if (vec) {
+        s_num[warp][d0] = acc.x;
+        s_num[warp][d0 + 1] = acc.y;
+        s_num[warp][d0 + 2] = acc.z;
+        s_num[warp][d0 + 3] = acc.w;
+      } else {
+        s_num[warp][d0] = acc.x;
+      }
+    }
+  }
+  if (lane == 0) s_den[warp] = den;
+  __syncthreads();
+  const float tot = s_den[0] + s_den[1] + s_den[2] + s_den[3];
+  auto final = [&](int d) {
+    const float num = s_num[0][d] + s_num[1][d] + s_num[2][d] + s_num[3][d];
+    return tot > 0.f ? num / tot : 0.f;
+  };
+  if (p.vec8) {
+    // 8 consecutive elements per thread: one 16-byte store per destination
+    for (int d0 = threadIdx.x * 8; d0 < p.D; d0 += NW * 32 * 8) {
+      float v8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v8[k] = final(d0 + k);
+      store_out8<T>(p, row, d0, v8);
+    }
+  } else {
+    for (int d = threadIdx.x; d < p.D; d += NW * 32) store_out<T>(p, row, d, final(d));
+  }
 }
 
 // ════════════════════════════════════════════════════════════════════════
@@ -749,6 +867,9 @@ __global__ void __launch_bounds__(32) pa_peer_barrier_kernel(PeerFlags f, unsign
                                                              int rank, int world, int* status,
                                                              unsigned long long budget_ns) {
   const int r = threadIdx.x;
+  // The next call's attention grid may become resident while this one waits
+  // (it waits for this grid itself before it reads anything).
+  pdl_launch_dependents();
   // Launched as a programmatic dependent: wait until the kernels that stored
   // this rank's rows (attention, then merge) have completed; their writes,
   // peer writes included, are flushed by then.
@@ -878,7 +999,7 @@ cudaError_t launch_ex(void (*kern)(KArgs...), unsigned grid, unsigned block, siz
 template <typename T, int DPL, int HG>
 cudaError_t launch_generic_t(const Params& p, cudaStream_t st) {
   const long long grid = (long long)p.B * p.Hkv * p.max_parts;
-  const bool pdl = p.after_append != 0;
+  const bool pdl = p.after_append != 0 || p.wait_first != 0;
   if constexpr (sizeof(T) == 2) {  // fp8 caches pair with fp16 queries
     if (p.kv_fmt == kKvE4M3)
       return launch_ex(pa_generic_kernel<T, DPL, HG, kKvE4M3>, (unsigned)grid, 128, 0, st, pdl, p);
@@ -967,7 +1088,8 @@ cudaError_t launch_fast_t(const CUtensorMap& tk, const CUtensorMap& tv, const Pa
   if (e != cudaSuccess) return e;
   const long long grid = (long long)p.B * p.Hkv * p.max_parts;
   return launch_ex(kern, (unsigned)grid, C::kThreads, C::kSmem, st,
-                   p.after_append != 0 || p.join_primary != 0, tk, tv, p);
+                   p.after_append != 0 || p.join_primary != 0 || p.wait_first != 0, tk, tv,
+                   p);
 }
 
 template <int D, int NT>
@@ -1009,10 +1131,16 @@ cudaError_t launch_fast(const CUtensorMap& tk, const CUtensorMap& tv, const Para
   }
 }
 
+// Rows with more partial slots than this are merged by four warps each.
+#ifndef XPA_WIDE_MERGE_SLOTS
+#define XPA_WIDE_MERGE_SLOTS 16
+#endif
+
 cudaError_t launch_reduce(const Params& p, int dtype_size, cudaStream_t st) {
   const long long rows = (long long)p.B * p.Hq;
+  const bool wide = p.slots > XPA_WIDE_MERGE_SLOTS;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((rows + 3) / 4));
+  cfg.gridDim = dim3((unsigned)(wide ? rows : (rows + 3) / 4));
   cfg.blockDim = dim3(128);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
@@ -1021,6 +1149,10 @@ cudaError_t launch_reduce(const Params& p, int dtype_size, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (wide) {
+    if (dtype_size == 4) return cudaLaunchKernelEx(&cfg, pa_reduce_wide_kernel<float>, p);
+    return cudaLaunchKernelEx(&cfg, pa_reduce_wide_kernel<__half>, p);
+  }
   if (dtype_size == 4) return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<float>, p);
   return cudaLaunchKernelEx(&cfg, pa_reduce_kernel<__half>, p);
 }
