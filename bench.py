@@ -76,10 +76,11 @@ def parse_args():
                     help="wall-time budget of the cpu_baseline leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the e2e leg (profiling runs)")
-    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+    ap.add_argument("--gather", choices=["fused", "fused-mc", "nccl"], default="fused",
                     help="N > 1: fused = kernels store each rank's heads into every GPU's "
-                         "buffer over NVLink (nxt_paged_attention_sharded); nccl = NCCL "
-                         "all-gather + head interleave")
+                         "buffer over NVLink (nxt_paged_attention_sharded); fused-mc = the same "
+                         "with one multimem (NVLS) store per row chunk into buffers from torch "
+                         "symmetric memory; nccl = NCCL all-gather + head interleave")
     ap.add_argument("--prefix", choices=["on", "off"], default="on",
                     help="c4: on = shared-prefix (cascade) attention over the radix prefix "
                          "groups (nxt_paged_attention_prefix_ex); off = plain decode kernels")
@@ -380,6 +381,7 @@ def cpu_leg(batch, arrays, seconds: float = 0.0, passes: int = 0, warmup: int = 
 # ── output check (outside the timed regions) ──────────────────────────────
 PARITY_RTOL = 1e-3  # north_star: 1e-3 relative error, fp32 accumulation
 _PARITY_OK = True    # set by the output check; a failed check makes the exit status 1
+_MC_ACTIVE = False   # --gather fused-mc found multicast support
 
 
 def parity_sample(num_seqs: int):
@@ -453,11 +455,13 @@ def run_ours(args, rank, world, local_rank):
     bt, sl = batch.tables_torch(dev)
     out = torch.empty_like(q)
     gathered = full = fg = None
-    fused = world > 1 and args.gather == "fused"
+    fused = world > 1 and args.gather in ("fused", "fused-mc")
     if fused:
         fg = sharding.FusedHeadGather(batch.num_seqs, batch.total_heads, batch.head_size,
                                       batch.dtype_size, world, rank, sharding.torch_exchange(),
-                                      dev)
+                                      dev, multicast=args.gather == "fused-mc")
+        global _MC_ACTIVE
+        _MC_ACTIVE = fg.multicast
     elif world > 1:
         gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
         full = torch.empty((batch.num_seqs, batch.total_heads, batch.head_size),
@@ -752,6 +756,13 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
                            (f"KV-head sharding x{world}, output gather fused into the kernels "
                             "(NVLink peer stores + bounded cross-GPU barrier)"
                             if args.gather == "fused" else
+                            f"KV-head sharding x{world}, output gather fused into the kernels "
+                            "(one multimem store per 16-byte chunk through NVSwitch multicast "
+                            "+ bounded cross-GPU barrier)"
+                            if args.gather == "fused-mc" and _MC_ACTIVE else
+                            f"KV-head sharding x{world}, output gather fused into the kernels "
+                            "(peer stores into symmetric-memory buffers; no multicast support) "
+                            "+ bounded cross-GPU barrier" if args.gather == "fused-mc" else
                             f"KV-head sharding x{world} + NCCL all-gather of outputs"),
             "l2": f"no flush: each step reads {tot_kv / world / 1e9:.2f} GB of KV per GPU "
                   f"(> {L2_BYTES >> 20} MB L2)",

@@ -450,12 +450,19 @@ size_t nxt_paged_attention_prefix_workspace_size(
  * [head_size] elements, then world_size uint64 flags), shares its IPC handle
  * with the others (any host-side channel) and opens theirs (nxt_pa_peer_open).
  * nxt_paged_attention_sharded then writes this rank's output heads directly
- * into every rank's buffer over NVLink peer stores (no collective library,
- * no multicast) and ends with a bounded cross-GPU barrier: when its stream
+ * into every rank's buffer over NVLink (no collective library) and ends with
+ * a bounded cross-GPU barrier: when its stream
  * reaches the end of step s, half (s & 1) of this rank's buffer holds the
  * whole [num_seqs][total_heads][head_size] output of step s from all ranks.
  * Consume that half before enqueueing step s + 2 on the same stream. A peer
- * that does not arrive within the wait budget raises NXT_PA_DEV_TIMEOUT. */
+ * that does not arrive within the wait budget raises NXT_PA_DEV_TIMEOUT.
+ *
+ * Rows are stored with one 16-byte store per peer, or, when mc_out is set,
+ * with one multimem store (NVLS) whose copies NVSwitch writes into every
+ * rank's buffer: mc_out is the multicast address of the gather buffers (a
+ * CUDA multicast object with every rank's buffer bound at the same offset,
+ * e.g. from torch symmetric memory), 16-byte aligned; NULL for peer stores.
+ * Only stores use it; nothing is ever loaded through it. */
 #define NXT_PA_MAX_PEERS 8
 #define NXT_PA_IPC_HANDLE_BYTES 64
 
@@ -466,6 +473,8 @@ typedef struct {
     int       head_offset;                   /* first query head of this rank */
     void     *peer_out[NXT_PA_MAX_PEERS];    /* rank r's gather buffer (opened) */
     uint64_t *peer_flags[NXT_PA_MAX_PEERS];  /* rank r's flag array (opened)  */
+    void     *mc_out;                        /* multicast address of the gather
+                                                buffers, or NULL              */
 } NxtPaShard;
 
 /* Allocates `bytes` of zero-filled device memory on the current device and

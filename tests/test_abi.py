@@ -197,8 +197,9 @@ int main(void) {
 
 def test_shard_descriptor_layout():
     from xllms_b200 import sharding as S
-    assert ctypes.sizeof(S.NxtPaShard) == 144
+    assert ctypes.sizeof(S.NxtPaShard) == 152
     assert S.NxtPaShard.peer_out.offset == 16 and S.NxtPaShard.peer_flags.offset == 80
+    assert S.NxtPaShard.mc_out.offset == 144
 
 
 def test_python_wrappers_refuse_bad_tensors_on_the_host():

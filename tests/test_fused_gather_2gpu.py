@@ -19,7 +19,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, multicast=False):
     import sys
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "tests"))
@@ -43,7 +43,8 @@ def _worker(rank, world, port, outdir):
         qs, ks, vs = (torch.from_numpy(x).to(dev) for x in
                       S.shard_heads(q, k, v, b.num_kv_heads, world, rank))
         bt, sl = b.tables_torch(dev)
-        fg = S.FusedHeadGather(b.num_seqs, 32, 128, 2, world, rank, S.torch_exchange(), dev)
+        fg = S.FusedHeadGather(b.num_seqs, 32, 128, 2, world, rank, S.torch_exchange(), dev,
+                               multicast=multicast)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
         for _ in range(4):
             out = fg.run(qs, ks, vs, bt, sl, b.scale, b.num_blocks, device_status=status)
@@ -57,13 +58,17 @@ def _worker(rank, world, port, outdir):
     np.save(os.path.join(outdir, f"rank{rank}.npy"), np.array(worst))
 
 
-def test_two_gpu_fused_gather(tmp_path):
+@pytest.mark.parametrize("multicast", [False, True], ids=["peer_stores", "multimem"])
+def test_two_gpu_fused_gather(tmp_path, multicast):
+    """peer_stores: IPC buffers, one store per peer. multimem: buffers from
+    torch symmetric memory, one multimem store per row chunk when the GPUs
+    support multicast (peer stores into the same buffers otherwise)."""
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    mp.start_processes(_worker, args=(2, _port(), str(tmp_path)), nprocs=2, start_method="spawn",
-                       join=True)
+    mp.start_processes(_worker, args=(2, _port(), str(tmp_path), multicast), nprocs=2,
+                       start_method="spawn", join=True)
     for r in range(2):
         res = np.load(tmp_path / f"rank{r}.npy")
         assert np.all(res[:-1] <= 1.0), res   # every step within tolerance

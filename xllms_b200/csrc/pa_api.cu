@@ -294,6 +294,7 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
       return NXT_PA_EINVAL;
     for (int r = 0; r < shard->world_size; ++r)
       if (!shard->peer_out[r] || !shard->peer_flags[r]) return NXT_PA_EINVAL;
+    if (reinterpret_cast<uintptr_t>(shard->mc_out) & 15u) return NXT_PA_EINVAL;
     out = shard->peer_out[shard->rank];
   }
   int rc = check_args(out, q, k, v, bt, sl, B, Hq, D, Hkv, max_blocks, bs, ds, kbs, khs);
@@ -429,6 +430,7 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
     p.head_offset = shard->head_offset;
     p.peer_off = (long long)(step & 1) * B * shard->total_heads * D;
     for (int r = 0; r < shard->world_size; ++r) p.peers[r] = shard->peer_out[r];
+    p.mc = shard->world_size > 1 ? shard->mc_out : nullptr;
   }
 
   cudaEvent_t ev_a = g_prof_before, ev_b = g_prof_after, ev_c = g_prof_merged;

@@ -47,6 +47,10 @@ struct Params {
   int npeers, Hq_total, head_offset;
   long long peer_off;
   void* peers[kMaxPeers];
+  // Multicast address of the peers' buffers (same element offsets), or null:
+  // with vec8, each 16-byte row chunk is then one multimem store that
+  // NVSwitch replicates into every peer's buffer.
+  void* mc;
   // 1 when D % 8 == 0 and out / peer buffers and the partial workspace are
   // 16-byte aligned: rows are then stored 8 elements (16 or 32 bytes) at a time.
   int vec8;
@@ -437,6 +441,15 @@ __device__ __forceinline__ void store_out(const Params& p, long long row, int d,
     if (r < p.npeers) static_cast<T*>(p.peers[r])[off] = x;
 }
 
+// One 16-byte store through a multicast address: NVSwitch writes it into
+// every buffer bound to the multicast object (relaxed, system scope; the
+// gather barrier's release / acquire orders it for the readers).
+__device__ __forceinline__ void multimem_st16(void* mc_addr, uint4 u) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr),
+               "r"(u.x), "r"(u.y), "r"(u.z), "r"(u.w)
+               : "memory");
+}
+
 // Stores elements d0 .. d0+7 of output row `row` with one 16-byte store (fp16)
 // or two (fp32) per destination. Requires Params::vec8.
 template <typename T>
@@ -459,11 +472,23 @@ __device__ __forceinline__ void store_out8(const Params& p, long long row, int d
       *reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + off) = u;
       return;
     }
+    if (p.mc) {
+      multimem_st16(static_cast<__half*>(p.mc) + off, u);
+      return;
+    }
 #pragma unroll
     for (int r = 0; r < kMaxPeers; ++r)
       if (r < p.npeers) *reinterpret_cast<uint4*>(static_cast<__half*>(p.peers[r]) + off) = u;
   } else {
     const float4 a = make_float4(v[0], v[1], v[2], v[3]), c = make_float4(v[4], v[5], v[6], v[7]);
+    if (p.npeers > 0 && p.mc) {
+      float* dst = static_cast<float*>(p.mc) + off;
+      multimem_st16(dst, make_uint4(__float_as_uint(a.x), __float_as_uint(a.y),
+                                    __float_as_uint(a.z), __float_as_uint(a.w)));
+      multimem_st16(dst + 4, make_uint4(__float_as_uint(c.x), __float_as_uint(c.y),
+                                        __float_as_uint(c.z), __float_as_uint(c.w)));
+      return;
+    }
     if (p.npeers == 0) {
       float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
       dst[0] = a;

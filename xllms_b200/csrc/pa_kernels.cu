@@ -529,6 +529,9 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
           mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
         }
         const float mn0 = fmaxf(mrun[nt][0], mx0), mn1 = fmaxf(mrun[nt][1], mx1);
+        // A running max that did not move gives alpha = 2^0 = 1 exactly, so
+        // when no lane's max moved the O rescale is skipped (bit-identical).
+        const bool moved = __any_sync(0xffffffffu, mn0 != mrun[nt][0] || mn1 != mrun[nt][1]);
         const float al0 = ex2(mrun[nt][0] - mn0), al1 = ex2(mrun[nt][1] - mn1);
         const float p0 = ex2(x0 - mn0), p1 = ex2(x1 - mn1);
         const float p2 = ex2(x2 - mn0), p3 = ex2(x3 - mn1);
@@ -536,12 +539,14 @@ __device__ __forceinline__ void tma_mma_body(const CUtensorMap& tmK, const CUten
         lrun[nt][1] = fmaf(lrun[nt][1], al1, p1 + p3);
         mrun[nt][0] = mn0;
         mrun[nt][1] = mn1;
+        if (moved) {
 #pragma unroll
-        for (int mt = 0; mt < C::kKSteps; ++mt) {
-          o[nt][mt][0] *= al0;
-          o[nt][mt][1] *= al1;
-          o[nt][mt][2] *= al0;
-          o[nt][mt][3] *= al1;
+          for (int mt = 0; mt < C::kKSteps; ++mt) {
+            o[nt][mt][0] *= al0;
+            o[nt][mt][1] *= al1;
+            o[nt][mt][2] *= al0;
+            o[nt][mt][3] *= al1;
+          }
         }
         // P^T as the B operand (k = token, n = head): transpose the
         // (token x head) accumulator pairs with movmatrix.

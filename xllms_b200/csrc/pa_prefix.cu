@@ -656,11 +656,22 @@ __global__ void __launch_bounds__(384, 1)
           for (int t = 0; t < 32; ++t) sr[t] = 0u;
         }
         const bool v0 = (vmask >> (2 * h)) & 1, v1 = (vmask >> (2 * h + 1)) & 1;
+        // A block whose 32 tokens of this half are all valid (the usual
+        // case inside a prefix) keeps its raw scores: no masking selects,
+        // the scale applied once to the maximum (a positive scale keeps the
+        // order) and folded into one FFMA before each ex2 below. The flag is
+        // the same for the whole warp.
+        const bool raw = v0 && v1 && lim >= 32 && sl2 > 0.f;
         float sv[32];
+        if (raw) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const bool valid = (t < 16 ? v0 : v1) && t < lim;
-          sv[t] = valid ? __uint_as_float(sr[t]) * sl2 : -INFINITY;
+          for (int t = 0; t < 32; ++t) sv[t] = __uint_as_float(sr[t]);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            const bool valid = (t < 16 ? v0 : v1) && t < lim;
+            sv[t] = valid ? __uint_as_float(sr[t]) * sl2 : -INFINITY;
+          }
         }
         float mx4[4];
 #pragma unroll
@@ -668,6 +679,7 @@ __global__ void __launch_bounds__(384, 1)
           mx4[q] = fmaxf(fmaxf(fmaxf(sv[q], sv[q + 4]), fmaxf(sv[q + 8], sv[q + 12])),
                          fmaxf(fmaxf(sv[q + 16], sv[q + 20]), fmaxf(sv[q + 24], sv[q + 28])));
         float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        if (raw) mx *= sl2;
         // combine with the other half of the row
         s_x[(b * 2 + h) * C::kRows + r] = mx;
         named_bar_sync(1 + q4, 64);
@@ -703,6 +715,8 @@ __global__ void __launch_bounds__(384, 1)
           if (!ok) continue;
         }
         const float mu = m_used == -INFINITY ? 0.f : m_used;  // all masked so far: P = 0
+        // raw scores: 2^(s * scale_log2 - mu) as one FFMA + ex2
+        const float ka = raw ? sl2 : 1.f;
         const uint32_t ph = sP + b * C::kPBuf + r * 128, pl = ph + C::kP;
         float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -711,7 +725,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int t = c * 8 + 2 * q;
-            const float p0 = ex2(sv[t] - mu), p1 = ex2(sv[t + 1] - mu);
+            const float p0 = ex2(fmaf(sv[t], ka, -mu)), p1 = ex2(fmaf(sv[t + 1], ka, -mu));
             ls[q] += p0 + p1;
             split_hi_lo(p0, p1, hi[q], lo[q]);
           }

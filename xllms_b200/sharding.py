@@ -69,6 +69,7 @@ class NxtPaShard(ctypes.Structure):
         ("head_offset", ctypes.c_int),
         ("peer_out", ctypes.c_void_p * 8),
         ("peer_flags", ctypes.c_void_p * 8),
+        ("mc_out", ctypes.c_void_p),
     ]
 
 
@@ -100,10 +101,19 @@ class FusedHeadGather:
     through `exchange` (e.g. torch_exchange()).
 
     run() enqueues step s and returns a [B, total_heads, D] view of half
-    (s & 1) of this rank's buffer, complete once the stream reaches it."""
+    (s & 1) of this rank's buffer, complete once the stream reaches it.
+
+    multicast=True takes the buffers from torch symmetric memory over `group`
+    (a torch.distributed process group; `exchange` is then unused) and, when
+    the GPUs support it, passes their NVLink multicast address so that each
+    16-byte row chunk leaves the GPU once and NVSwitch writes it into every
+    rank's buffer (`self.multicast` says whether that address exists).
+    Failure tests keep the default: a rank that dies while its memory is
+    bound to a multicast object can fault its peers' GPUs."""
 
     def __init__(self, num_seqs: int, total_heads: int, head_size: int, dtype_size: int,
-                 world_size: int, rank: int, exchange, device=None):
+                 world_size: int, rank: int, exchange, device=None, multicast: bool = False,
+                 group=None):
         from . import _native
         self.lib = _native.xpa()
         self.B, self.H, self.D, self.es = num_seqs, total_heads, head_size, dtype_size
@@ -114,39 +124,73 @@ class FusedHeadGather:
         self.half_bytes = half
         self.flags_off = (2 * half + 255) // 256 * 256
         total = self.flags_off + 8 * world_size
-        own = ctypes.c_void_p()
-        handle = (ctypes.c_char * _native.NXT_PA_IPC_HANDLE_BYTES)()
-        rc = self.lib.nxt_pa_peer_alloc(total, ctypes.byref(own), handle)
-        if rc != 0:
-            raise RuntimeError(f"nxt_pa_peer_alloc: {_native.strerror(rc)}")
-        self.own = own.value
-        handles = exchange(bytes(handle))
         self.opened = []
+        self.own = 0
+        self.symm = None
+        self.multicast = False
         self.shard = NxtPaShard()
         self.shard.world_size, self.shard.rank = world_size, rank
         self.shard.total_heads = total_heads
         self.shard.head_offset = rank * (total_heads // world_size)
-        for r in range(world_size):
-            if r == rank:
-                base = self.own
-            else:
-                p = ctypes.c_void_p()
-                rc = self.lib.nxt_pa_peer_open(handles[r], ctypes.byref(p))
-                if rc != 0:
-                    raise RuntimeError(f"nxt_pa_peer_open(rank {r}): {_native.strerror(rc)}")
-                base = p.value
-                self.opened.append(base)
-            self.shard.peer_out[r] = base
-            self.shard.peer_flags[r] = base + self.flags_off
+        if multicast:
+            bases, mc = self._symmetric(total, device, group)
+            for r in range(world_size):
+                self.shard.peer_out[r] = bases[r]
+                self.shard.peer_flags[r] = bases[r] + self.flags_off
+            self.shard.mc_out = mc or None
+            self.multicast = bool(mc)
+            base_own = bases[rank]
+        else:
+            own = ctypes.c_void_p()
+            handle = (ctypes.c_char * _native.NXT_PA_IPC_HANDLE_BYTES)()
+            rc = self.lib.nxt_pa_peer_alloc(total, ctypes.byref(own), handle)
+            if rc != 0:
+                raise RuntimeError(f"nxt_pa_peer_alloc: {_native.strerror(rc)}")
+            self.own = own.value
+            base_own = self.own
+            handles = exchange(bytes(handle))
+            for r in range(world_size):
+                if r == rank:
+                    base = self.own
+                else:
+                    p = ctypes.c_void_p()
+                    rc = self.lib.nxt_pa_peer_open(handles[r], ctypes.byref(p))
+                    if rc != 0:
+                        raise RuntimeError(f"nxt_pa_peer_open(rank {r}): {_native.strerror(rc)}")
+                    base = p.value
+                    self.opened.append(base)
+                self.shard.peer_out[r] = base
+                self.shard.peer_flags[r] = base + self.flags_off
         self.step = 0
         self.device = device
         # Views of the two halves, made once: importing device memory into
         # torch per step would cost host time on every step.
         import torch
         typestr = "<f2" if self.es == 2 else "<f4"
-        self.views = [torch.as_tensor(_DeviceArray(self.own + i * self.half_bytes,
+        self.views = [torch.as_tensor(_DeviceArray(base_own + i * self.half_bytes,
                                                    (self.B, self.H, self.D), typestr),
                                       device=device) for i in (0, 1)]
+
+    def _symmetric(self, nbytes, device, group):
+        """Buffers from torch symmetric memory: every rank's base address as
+        mapped here, and the multicast address (0 when unsupported)."""
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        group = group or dist.group.WORLD
+        self.symm = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        self.symm.zero_()
+        torch.cuda.synchronize(device)
+        hdl = symm_mem.rendezvous(self.symm, group)
+        self.symm_handle = hdl
+        off = self.symm.data_ptr() - int(hdl.buffer_ptrs[self.rank])
+        bases = [int(x) + off for x in hdl.buffer_ptrs]
+        idx = torch.device(device).index if device is not None else torch.cuda.current_device()
+        supported = symm_mem._SymmetricMemory.has_multicast_support(symm_mem.DeviceType.CUDA,
+                                                                     idx or 0)
+        mc = int(hdl.multicast_ptr) if supported else 0
+        dist.barrier(group)
+        return bases, (mc + off) if mc else 0
 
     def output(self, step: int):
         """[B, total_heads, D] view of the half that holds step `step`."""
@@ -204,3 +248,5 @@ class FusedHeadGather:
         if self.own:
             self.lib.nxt_pa_peer_free(self.own)
             self.own = 0
+        self.symm_handle = None
+        self.symm = None
