@@ -88,8 +88,8 @@ def parse_args():
                     help="1 GPU, c2/c5: run rank 0's shard of the P-GPU workload alone, with no "
                          "gather (the per-GPU work of a P-GPU run without its exchange)")
     ap.add_argument("--seed", type=int, default=None,
-                    help="c2/c5: another seed for the lengths, tables and values of the "
-                         "workload (default: the configuration's own)")
+                    help="another seed for the lengths, tables and values of the workload "
+                         "(default: the configuration's own)")
     ap.add_argument("--seqs", type=int, default=0,
                     help="sequences per GPU for c2/c4/c5 (default: the BASELINE size); smaller "
                          "values make the small cases the ncu captures run on")
@@ -142,9 +142,11 @@ def make_batch(workload: str, world: int, rank: int, seqs: int = 0, seed=None):
         return W.config5(world_size=world, rank=rank, num_seqs=seqs or 512, **kw)
     if world > 1:
         raise SystemExit(f"workload {workload} runs on one GPU")
-    if workload == "c4" and seqs:
-        return W.config4(num_seqs=seqs)
-    return W.CONFIGS[workload]()
+    if workload == "c4":
+        return W.config4(num_seqs=seqs or 256, **kw)
+    if workload == "c3":
+        return W.config3(**kw)
+    return W.CONFIGS[workload](**kw)
 
 
 # ── clocks during the timed region ────────────────────────────────────────
@@ -457,9 +459,15 @@ def run_ours(args, rank, world, local_rank):
     gathered = full = fg = None
     fused = world > 1 and args.gather in ("fused", "fused-mc")
     if fused:
+        want_mc = args.gather == "fused-mc"
+        if want_mc:
+            # every rank must take the same path: agree on multicast support first
+            ok = torch.tensor([1 if sharding.multicast_supported(dev) else 0], device=dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            want_mc = bool(ok.item())
         fg = sharding.FusedHeadGather(batch.num_seqs, batch.total_heads, batch.head_size,
                                       batch.dtype_size, world, rank, sharding.torch_exchange(),
-                                      dev, multicast=args.gather == "fused-mc")
+                                      dev, multicast=want_mc)
         global _MC_ACTIVE
         _MC_ACTIVE = fg.multicast
     elif world > 1:

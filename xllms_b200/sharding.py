@@ -93,6 +93,19 @@ def torch_exchange(group=None):
     return exchange
 
 
+def multicast_supported(device) -> bool:
+    """Whether torch symmetric memory can give an NVLink multicast address
+    on `device` (False when the query itself is unavailable)."""
+    try:
+        import torch
+        import torch.distributed._symmetric_memory as symm_mem
+        idx = torch.device(device).index
+        return bool(symm_mem._SymmetricMemory.has_multicast_support(
+            symm_mem.DeviceType.CUDA, idx if idx is not None else torch.cuda.current_device()))
+    except Exception:
+        return False
+
+
 class FusedHeadGather:
     """KV-head-sharded decode attention whose output all-gather is fused into
     the kernels (nxt_paged_attention_sharded): each rank's kernels store its
@@ -185,10 +198,8 @@ class FusedHeadGather:
         self.symm_handle = hdl
         off = self.symm.data_ptr() - int(hdl.buffer_ptrs[self.rank])
         bases = [int(x) + off for x in hdl.buffer_ptrs]
-        idx = torch.device(device).index if device is not None else torch.cuda.current_device()
-        supported = symm_mem._SymmetricMemory.has_multicast_support(symm_mem.DeviceType.CUDA,
-                                                                     idx or 0)
-        mc = int(hdl.multicast_ptr) if supported else 0
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        mc = int(hdl.multicast_ptr) if multicast_supported(dev) else 0
         dist.barrier(group)
         return bases, (mc + off) if mc else 0
 
