@@ -230,3 +230,25 @@ def test_python_wrappers_refuse_bad_tensors_on_the_host():
         with pytest.raises(PA.PagedAttentionError) as ei:
             call()
         assert ei.value.code == _native.NXT_PA_EINVAL, i
+
+
+def test_sharded_call_refuses_a_misaligned_multicast_address():
+    """The multicast address of the gather buffers takes 16-byte stores: a
+    misaligned one is refused with NXT_PA_EINVAL before anything touches a
+    device (and so is a shard without peer buffers)."""
+    from xllms_b200 import sharding as S
+    lib = _native.xpa()
+    sh = S.NxtPaShard()
+    sh.world_size, sh.rank, sh.total_heads, sh.head_offset = 2, 0, 32, 0
+    for r in range(2):
+        sh.peer_out[r] = 1 << 20
+        sh.peer_flags[r] = (1 << 20) + 4096
+    p = ctypes.c_void_p(4096)
+    ip = ctypes.cast(p, ctypes.POINTER(ctypes.c_int))
+    args = (1, p, p, p, ip, ip, 2, 16, 128, 4, 0.088, 4, 16, 2, 4 * 16 * 128, 16 * 128, 64,
+            None, None)
+    sh.mc_out = (1 << 21) + 8
+    assert lib.nxt_paged_attention_sharded(ctypes.byref(sh), *args) == _native.NXT_PA_EINVAL
+    sh.mc_out = None
+    sh.peer_out[1] = None
+    assert lib.nxt_paged_attention_sharded(ctypes.byref(sh), *args) == _native.NXT_PA_EINVAL
