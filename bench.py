@@ -609,46 +609,57 @@ def run_ours(args, rank, world, local_rank):
         host_parts += [torch.from_numpy(a) for a in
                        PA.PrefixGroups.host_arrays(batch.prefix_groups, batch.num_seqs)]
     sizes = [t.numel() * t.element_size() for t in host_parts]
-    stage_h = torch.empty(sum(sizes), dtype=torch.uint8).pin_memory()
-    stage_d = torch.empty_like(stage_h, device=dev)
-    views, o = [], 0
-    for t, n in zip(host_parts, sizes):
-        stage_h[o:o + n].copy_(t.reshape(-1).view(torch.uint8))
-        views.append(stage_d[o:o + n].view(t.dtype).view(t.shape))
-        o += n
-    q_d, bt_d, sl_d = views[:3]
-    groups_d = None
-    if cascade:
-        groups_d = PA.PrefixGroups(batch.prefix_groups, batch.num_seqs, prefix_pages=views[3],
-                                   offsets=views[4], members=views[5])
-    out_d = torch.empty_like(out)
-    res = full if (world > 1 and not fused) else out_d
-    out_h = torch.empty((batch.num_seqs, batch.total_heads, batch.head_size),
-                        dtype=out.dtype).pin_memory()
-    pa_in = None if fp8 else PA.make_input(q_d, k, v, bt_d, sl_d, scale=batch.scale,
-                                           stream=torch.cuda.current_stream())
 
-    def e2e_step():
-        stage_d.copy_(stage_h, non_blocking=True)
+    def make_io():
+        """Pinned host staging + its device copy (viewed as the step's input
+        tensors), a device output and a pinned host output."""
+        io = {"stage_h": torch.empty(sum(sizes), dtype=torch.uint8).pin_memory()}
+        io["stage_d"] = torch.empty_like(io["stage_h"], device=dev)
+        views, o = [], 0
+        for t, n in zip(host_parts, sizes):
+            io["stage_h"][o:o + n].copy_(t.reshape(-1).view(torch.uint8))
+            views.append(io["stage_d"][o:o + n].view(t.dtype).view(t.shape))
+            o += n
+        io["q"], io["bt"], io["sl"] = views[:3]
+        io["groups"] = (PA.PrefixGroups(batch.prefix_groups, batch.num_seqs,
+                                        prefix_pages=views[3], offsets=views[4],
+                                        members=views[5]) if cascade else None)
+        io["out_d"] = torch.empty_like(out)
+        io["out_h"] = torch.empty((batch.num_seqs, batch.total_heads, batch.head_size),
+                                  dtype=out.dtype).pin_memory()
+        io["pa_in"] = None if fp8 else PA.make_input(io["q"], k, v, io["bt"], io["sl"],
+                                                     scale=batch.scale,
+                                                     stream=torch.cuda.current_stream())
+        return io
+
+    io0 = make_io()
+    stage_h, out_h = io0["stage_h"], io0["out_h"]
+
+    def compute(io):
+        """One step through the C ABI on the current stream; returns the
+        device tensor that holds its [B, Hq_total, D] result."""
         if fused:
             # the C-ABI sharded entry point (the plugin descriptor has no shard fields)
-            out_h.copy_(fg.run(q_d, k, v, bt_d, sl_d, batch.scale, batch.num_blocks),
-                        non_blocking=True)
-            return
+            return fg.run(io["q"], k, v, io["bt"], io["sl"], batch.scale, batch.num_blocks)
         if cascade:
             # the C-ABI cascade entry point (the plugin descriptor has no group fields)
-            PA.paged_attention_prefix(q_d, k, v, bt_d, sl_d, groups_d, out=out_d,
-                                      num_blocks=batch.num_blocks)
+            PA.paged_attention_prefix(io["q"], k, v, io["bt"], io["sl"], io["groups"],
+                                      out=io["out_d"], num_blocks=batch.num_blocks)
         elif fp8:
             # the C-ABI fp8 entry point (the plugin descriptor has no KV format)
-            PA.paged_attention_fp8(q_d, k, v, bt_d, sl_d, args.kv, k_scale, v_scale, out=out_d,
-                                   num_blocks=batch.num_blocks)
-        elif plugin.run(pa_in, out_d) != 0:
+            PA.paged_attention_fp8(io["q"], k, v, io["bt"], io["sl"], args.kv, k_scale, v_scale,
+                                   out=io["out_d"], num_blocks=batch.num_blocks)
+        elif plugin.run(io["pa_in"], io["out_d"]) != 0:
             raise SystemExit("nxt_backend_run failed")
         if world > 1:
-            sharding.gather_heads(out_d, gathered)
+            sharding.gather_heads(io["out_d"], gathered)
             sharding.interleave_heads(gathered, full)
-        out_h.copy_(res, non_blocking=True)
+            return full
+        return io["out_d"]
+
+    def e2e_step():
+        io0["stage_d"].copy_(io0["stage_h"], non_blocking=True)
+        io0["out_h"].copy_(compute(io0), non_blocking=True)
 
     for _ in range(max(3, args.warmup)):
         e2e_step()
@@ -674,6 +685,55 @@ def run_ours(args, rank, world, local_rank):
     h_stop.record()
     torch.cuda.nvtx.range_pop()
     barrier()
+    # Pipelined (1 GPU): two input / output sets; a step's host->device copy
+    # runs on its own stream during the previous step's compute and its
+    # device->host read during the next step's, as a serving loop overlaps
+    # them. Every copy of every step is still inside the timed region.
+    t_e2e_pipe = None
+    if world == 1:
+        ios = [io0, make_io()]
+        comp, up, down = torch.cuda.current_stream(), torch.cuda.Stream(), torch.cuda.Stream()
+        up_done = [torch.cuda.Event() for _ in range(2)]
+        comp_done = [torch.cuda.Event() for _ in range(2)]
+        down_done = [torch.cuda.Event() for _ in range(2)]
+
+        def piped(n, t_start=None, t_stop=None):
+            if t_start is not None:
+                t_start.record(comp)
+            up.wait_stream(comp)
+            down.wait_stream(comp)
+            for i in range(n):
+                b, io = i & 1, ios[i & 1]
+                with torch.cuda.stream(up):
+                    if i >= 2:
+                        up.wait_event(comp_done[b])  # set b's inputs consumed
+                    io["stage_d"].copy_(io["stage_h"], non_blocking=True)
+                    up_done[b].record(up)
+                comp.wait_event(up_done[b])
+                if i >= 2:
+                    comp.wait_event(down_done[b])  # set b's output read back
+                res_d = compute(io)
+                comp_done[b].record(comp)
+                with torch.cuda.stream(down):
+                    down.wait_event(comp_done[b])
+                    io["out_h"].copy_(res_d, non_blocking=True)
+                    down_done[b].record(down)
+            comp.wait_stream(down)
+            if t_stop is not None:
+                t_stop.record(comp)
+
+        piped(max(3, args.warmup))
+        barrier()
+        p_start = torch.cuda.Event(enable_timing=True)
+        p_stop = torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("e2e pipelined steps")
+        piped(K, p_start, p_stop)
+        torch.cuda.nvtx.range_pop()
+        barrier()
+        t_e2e_pipe = p_start.elapsed_time(p_stop) / K
+        for io in ios:
+            if not torch.equal(io["out_h"].to(dev), resident):
+                raise SystemExit("pipelined e2e output differs from the device-resident run")
     sampler.close()
     clocks, clocks_e2e = sampler.summary(c0, c1), sampler.summary(e0, e1)
     t_e2e = e_start.elapsed_time(e_stop) / K
@@ -687,12 +747,12 @@ def run_ours(args, rank, world, local_rank):
     d2h = out_h.numel() * out_h.element_size()
     return _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t_e2e,
                    clocks, clocks_e2e, q, k, v, h2d, d2h, dev, cascade, parity=parity,
-                   split=split, t_e2e_sync=t_e2e_sync)
+                   split=split, t_e2e_sync=t_e2e_sync, t_e2e_pipe=t_e2e_pipe)
 
 
 def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t_e2e, clocks,
             clocks_e2e, q, k, v, h2d, d2h, dev, cascade=False, parity=(True, 0.0), split=None,
-            t_e2e_sync=None):
+            t_e2e_sync=None, t_e2e_pipe=None):
     import torch
     import torch.distributed as dist
     K = args.steps
@@ -720,6 +780,7 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
         tot_bytes, tot_ub, tot_kv, h2d, d2h = (float(x) for x in s.tolist())
     else:
         tot_bytes, tot_ub, tot_kv = float(bytes_rank), float(ub_rank), float(kv_rank)
+    t_e2e_best = min(x for x in (t_e2e, t_e2e_pipe) if x) if t_e2e else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -804,11 +865,27 @@ def _finish(args, rank, world, batch, path, launches_per_step, t_step, t_kern, t
             "bytes_per_launch": ub_rank,
         },
         "e2e": None if t_e2e is None else {
-            "value": round(tot_bytes / (t_e2e * 1e-3) / 1e9, 2),
+            "value": round(tot_bytes / (t_e2e_best * 1e-3) / 1e9, 2),
             "unit": "GB/s",
-            "ms_per_step": round(t_e2e, 5),
+            "ms_per_step": round(t_e2e_best, 5),
             "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h),
+            "timing": ("the faster of two ways to run the steps, every copy of every step inside "
+                       "the timed region: " + ("pipelined" if t_e2e_best == t_e2e_pipe else
+                                               "enqueued") + " (both below)"),
+            "enqueued": {
+                "value": round(tot_bytes / (t_e2e * 1e-3) / 1e9, 2),
+                "ms_per_step": round(t_e2e, 5),
+                "what": "one input / output set, copies and compute in stream order, steps "
+                        "enqueued back to back",
+            },
+            "pipelined": None if t_e2e_pipe is None else {
+                "value": round(tot_bytes / (t_e2e_pipe * 1e-3) / 1e9, 2),
+                "ms_per_step": round(t_e2e_pipe, 5),
+                "what": "two input / output sets; each step's H2D copy runs on its own stream "
+                        "during the previous step's compute and its D2H read during the next "
+                        "step's (1 GPU)",
+            },
             "api": ("nxt_paged_attention_prefix_ex (libxpa.so); per step one pinned H2D copy "
                     "(Q, block tables, seq_lens, prefix groups) and one D2H copy of the output"
                     if cascade else
