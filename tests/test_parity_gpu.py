@@ -317,3 +317,31 @@ def test_index_logic_bit_exact(cuda, head_size, dtype, group, block_size):
     out = PA.paged_attention(qt, kt, vt, bt, sl, num_blocks=b.num_blocks)
     assert PA.device_status() == 0
     assert_hot_cells(out, expect)
+
+
+def test_inputs_written_by_the_previous_kernel(cuda):
+    """The first kernel of a call is launched as a programmatic dependent of
+    whatever kernel precedes it on the stream and waits for it before reading
+    anything: query, pools and tables written by kernels right before the call
+    (no synchronisation in between) must be the ones the call sees."""
+    import torch
+    b = W.make_batch("prev", [3000, 17, 700, 1], 32, 8, 128, "f16", 57, value_std=0.5)
+    q, k, v = b.values_numpy()
+    ref = oracle_out(b, q, k, v)
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    out = torch.empty_like(qt)
+    q_stale, k_stale = torch.zeros_like(qt), torch.zeros_like(kt)
+    bt_stale, sl_stale = torch.zeros_like(bt), torch.zeros_like(sl)
+    for _ in range(3):
+        # kernels (not copies) overwrite every input just before the call
+        q_stale.mul_(0).add_(qt)
+        k_stale.mul_(0).add_(kt)
+        bt_stale.mul_(0).add_(bt)
+        sl_stale.mul_(0).add_(sl)
+        PA.paged_attention(q_stale, k_stale, vt, bt_stale, sl_stale, out=out,
+                           num_blocks=b.num_blocks)
+        check_close(out, ref, what="inputs written by the preceding kernels")
+        q_stale.zero_()
+        k_stale.zero_()
+        sl_stale.zero_()
+    assert PA.device_status() == 0
