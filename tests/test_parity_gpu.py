@@ -244,6 +244,45 @@ def test_caller_workspace_and_stream(cuda):
     assert int(status.item()) == 0
 
 
+def test_per_thread_default_streams_of_two_threads(cuda):
+    """cudaStreamPerThread is one handle for every host thread but a separate
+    stream in each: two threads calling at once on it must not share the
+    library's split-context workspace."""
+    import threading
+    import torch
+    per_thread = 2  # cudaStreamPerThread
+    inputs, refs = [], []
+    for i, lens in enumerate(([9000, 4100, 7000, 300], [5000, 8192, 2500, 6000])):
+        b = W.make_batch(f"pt{i}", lens * 4, 32, 8, 128, "f16", 60 + i)
+        q, k, v = b.values_numpy()
+        x = to_device(b, q, k, v, cuda)
+        inputs.append(x)
+        refs.append(PA.paged_attention(*x))
+    torch.cuda.synchronize()
+    outs = [[], []]
+    errors = []
+
+    def worker(i):
+        try:
+            for _ in range(20):
+                outs[i].append(PA.paged_attention(*inputs[i], stream=per_thread))
+        except Exception as e:  # reported below, on the test's thread
+            errors.append(e)
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in (0, 1)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    torch.cuda.synchronize()
+    assert not errors, errors
+    for i in (0, 1):
+        assert len(outs[i]) == 20
+        for o in outs[i]:
+            assert torch.equal(o, refs[i])
+    assert PA.device_status() == 0
+
+
 def test_repeatable_bitwise(cuda):
     b = W.make_batch("d", [777, 4000], 32, 8, 128, "f16", 53)
     q, k, v = b.values_numpy()

@@ -11,6 +11,8 @@
 #include <algorithm>
 #include <cmath>
 #include <mutex>
+#include <thread>
+#include <functional>
 #include <utility>
 
 #include "operator_api.h"
@@ -41,6 +43,16 @@ struct DeviceState {
   int* status = nullptr;  // library status word
 };
 DeviceState g_dev[kMaxDevices];
+
+// Map key of a stream. The per-thread default stream has one handle for
+// every host thread but is a different stream in each, so it is told apart
+// by the thread.
+uintptr_t stream_key(cudaStream_t st) {
+  if (st == cudaStreamPerThread)
+    return (static_cast<uintptr_t>(std::hash<std::thread::id>{}(std::this_thread::get_id()))
+            << 4) | 0xfu;
+  return reinterpret_cast<uintptr_t>(st);
+}
 
 struct Workspace {
   void* ptr = nullptr;  // split-context partials
@@ -365,7 +377,7 @@ int run(void* out, const void* q, const void* k, const void* v, const int* bt, c
     if (ws) {
       if (ws_bytes < pl.ws_bytes) return NXT_PA_EWORKSPACE;
     } else {
-      Workspace& w = g_ws[{dev, reinterpret_cast<uintptr_t>(st)}];
+      Workspace& w = g_ws[{dev, stream_key(st)}];
       if (w.bytes < pl.ws_bytes) {
         if (w.ptr) cudaFree(w.ptr);  // synchronises: no kernel still reads it
         w.ptr = nullptr;
