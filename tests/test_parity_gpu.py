@@ -244,10 +244,42 @@ def test_caller_workspace_and_stream(cuda):
     assert int(status.item()) == 0
 
 
+def test_first_call_of_a_fresh_host_thread(cuda):
+    """A host thread whose first CUDA call is the library's has no current
+    context yet: the call must still take the TMA path (not fall back to the
+    CUDA-core kernel) and give the same bits as any other thread."""
+    import threading
+    import torch
+    b = W.make_batch("fresh", [3000, 70, 9000], 32, 8, 128, "f16", 59)
+    q, k, v = b.values_numpy()
+    qt, kt, vt, bt, sl = to_device(b, q, k, v, cuda)
+    ref = PA.paged_attention(qt, kt, vt, bt, sl)
+    out = torch.empty_like(ref)
+    torch.cuda.synchronize()
+    seen = {}
+
+    def worker():
+        try:
+            seen["path"] = PA.kernel_path(kt, vt, 32, 128, 8, 16, 2, b.kv_block_stride,
+                                          b.kv_head_stride)
+            PA.paged_attention(qt, kt, vt, bt, sl, out=out, stream=2)  # cudaStreamPerThread
+        except Exception as e:  # reported below, on the test's thread
+            seen["error"] = e
+
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join()
+    torch.cuda.synchronize()
+    assert "error" not in seen, seen
+    assert seen["path"] == _native.NXT_PA_PATH_TMA_MMA
+    assert torch.equal(out, ref)
+
+
 def test_per_thread_default_streams_of_two_threads(cuda):
     """cudaStreamPerThread is one handle for every host thread but a separate
     stream in each: two threads calling at once on it must not share the
-    library's split-context workspace."""
+    library's split-context workspace, and each thread's first call (no
+    current context yet) must take the same path as the rest."""
     import threading
     import torch
     per_thread = 2  # cudaStreamPerThread

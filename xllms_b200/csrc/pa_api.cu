@@ -199,9 +199,20 @@ bool encode_pool(CUtensorMap* m, const void* base, int D, int Hkv, long long num
   cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   const CUtensorMapDataType dt =
       es == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUresult r = fn(m, dt, 4, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  auto encode = [&] {
+    return fn(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = encode();
+  if (r != CUDA_SUCCESS) {
+    // A host thread whose first CUDA call this is has no current context
+    // yet, and the driver call fails without one: bind the current device's
+    // primary context (what the runtime's own first call would do) and
+    // encode again, so that such a call still takes the TMA path.
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) r = encode();
+  }
   return r == CUDA_SUCCESS;
 }
 
