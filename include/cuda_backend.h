@@ -57,7 +57,12 @@ int nxt_backend_init(NxtBackend *backend);
 int nxt_backend_run(NxtBackend *backend, void *input, void *output);
 
 /* Replaces nxt_backend_fini (reference backends/cuda_backend.c:108-120):
- * -1 on NULL; frees the plugin state, sets state UNINITIALIZED, returns 0. */
+ * -1 on NULL; frees the plugin state and the workspaces and status words
+ * libxpa.so allocated on first use (nxt_paged_attention_release_workspaces,
+ * which synchronises each device that holds one), sets state UNINITIALIZED,
+ * returns 0 (-1 if a CUDA call of that release failed). A later call of any
+ * entry point allocates them again. The reference process holds one CUDA
+ * backend, so its fini is the end of the library's use. */
 int nxt_backend_fini(NxtBackend *backend);
 
 #ifdef __cplusplus

@@ -214,6 +214,12 @@ void nxt_paged_attention(void *out, const void *query, const void *key_cache,
 
 int nxt_paged_attention_last_error(void) { return NXT_PA_OK; }
 
+static int g_releases;
+int nxt_paged_attention_release_workspaces(void) {
+    g_releases++;
+    return NXT_PA_OK;
+}
+
 static void check_plugin(void) {
     CHECK(nxt_backend_init(NULL) == -1);
     CHECK(nxt_backend_run(NULL, NULL, NULL) == -1);
@@ -248,6 +254,7 @@ static void check_plugin(void) {
                      offsetof(NxtPagedAttentionInput, num_seqs)) == 0);
     CHECK(nxt_backend_fini(&be) == 0);
     CHECK(be.state == NXT_BACKEND_STATE_UNINITIALIZED && be.backend_state == NULL);
+    CHECK(g_releases == 1); /* fini hands the library's workspaces back */
 }
 
 int main(void) {

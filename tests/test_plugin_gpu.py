@@ -35,6 +35,16 @@ def test_plugin_init_run_fini(cuda):
     assert plug.close() == 0
     assert plug.backend.state == PA.NXT_BACKEND_STATE_UNINITIALIZED
     assert plug.run(pa, out) == -1  # state freed
+    # fini released the library's workspaces and status words: the next
+    # backend (and any direct call) allocates them again
+    again = PA.CudaBackendPlugin()
+    out.fill_(float("nan"))
+    assert again.run(pa, out) == 0
+    torch.cuda.synchronize()
+    check_close(out, ref, what="plugin after fini")
+    check_close(PA.paged_attention(qt, kt, vt, bt, sl), ref, what="direct call after fini")
+    assert PA.device_status() == 0
+    assert again.close() == 0
 
 
 def test_reference_smoke_calls(cuda):

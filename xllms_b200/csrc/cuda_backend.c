@@ -53,5 +53,7 @@ int nxt_backend_fini(NxtBackend *backend) {
     free(backend->backend_state);
     backend->backend_state = NULL;
     backend->state = NXT_BACKEND_STATE_UNINITIALIZED;
-    return 0;
+    /* the split-context workspaces and status words the attention calls
+     * allocated lazily go with the backend */
+    return nxt_paged_attention_release_workspaces() == NXT_PA_OK ? 0 : -1;
 }
